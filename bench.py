@@ -1,0 +1,456 @@
+"""Benchmark of the decode-matmul hot path on B200.
+
+Headline (one JSON line on rank 0): the fused fp16 lm_head GEMV + greedy
+argmax over the 248,094-row vocabulary (K=1024, M=1), sharded over N GPUs
+(contiguous vocab rows per rank, one NCCL max all-reduce of the 64-bit argmax
+key).  value = microseconds per lm_head+argmax for the whole job (max over
+ranks, lower is better, strong scaling: the vocabulary is fixed).
+
+At N=1 the same line also carries the other measured configurations:
+  w4a16_gemv   config 0 (M=1, K=1024, N=3584) in GB/s and % of HBM peak
+  w8a8         config 2 (M in {1,4,8}, N in {1024,3584})
+  decode_step  config 3 (186 W4A16 GEMVs + the lm_head per token)
+
+Timing: W warm-up steps, then exactly K steps captured in one CUDA graph and
+replayed once between barrier + synchronize; CUDA events on the launching
+stream; max over ranks.  Inputs exceed L2: each step reads a different copy of
+the (shard) weight, with enough copies to cover at least twice the L2 size.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "minicpm-v-4.6-orangepi_b200")
+for _p in (PKG, os.path.join(ROOT, "oracle")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+
+K_HIDDEN = 1024
+VOCAB = 248094
+METRIC = "lm_head+argmax latency (fp16, K=1024, V=248094, M=1)"
+WORKLOAD = "config1: fp16 lm_head GEMV M=1 K=1024 N=248094 fused greedy argmax, vocab-sharded over n_gpus"
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def load_traffic():
+    """dram bytes per launch per kernel from the committed ncu summary."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while a region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"mcv_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = float(parts[2])
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------
+# reference arm: the CPU implementation of the path (the oracle port)
+# ----------------------------------------------------------------------------
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import oracle
+    from mcv_b200 import synth
+    nthreads = os.cpu_count() or 1
+    x, w = synth.lm_head_inputs(K_HIDDEN, VOCAB, seed=1)
+    for _ in range(args.warmup):
+        oracle.lm_head_argmax(x, w, nthreads=nthreads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.lm_head_argmax(x, w, nthreads=nthreads)
+    dt = (time.perf_counter() - t0) / args.steps
+    us = dt * 1e6
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(us, 2), "unit": "us", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic", "config": {"workload": WORKLOAD},
+        "cpu_baseline": {"value": round(us, 2), "unit": "us", "cores": nthreads, "kind": "port",
+                         "sample": "full 248094-row vocab per step: fp32 dot over ascending k and strict '>' "
+                                   "first-max argmax (tests/test_lm_head_pipeline.cpp:95-107), "
+                                   f"rows split over {nthreads} threads"},
+        "e2e": {"value": round(us, 2), "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------
+# GPU arm
+# ----------------------------------------------------------------------------
+
+def graph_of(torch, fn, stream):
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn()
+    return g
+
+
+def time_graph_ms(torch, g, reps=1):
+    s = torch.cuda.current_stream()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(reps):
+        g.replay()
+    e1.record(s)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def rand_f16(torch, shape, std, gen):
+    return (torch.randn(shape, generator=gen, device="cuda", dtype=torch.float32) * std).to(torch.float16)
+
+
+def bench_w4a16_gemv(torch, mcv, synth, l2, hbm):
+    M, K, N = 1, 1024, 3584
+    x, q, z, s = synth.w4a16_inputs(M, K, N, seed=0)
+    w0 = mcv.pack_w4a16(q, z, s)
+    per = synth.w4a16_bytes(M, K, N)
+    copies = max(2, int(np.ceil(2 * l2 / w0.nbytes)))
+    ws = [w0] + [mcv.W4A16QuantizedWeight(w0.qweight.clone(), w0.scales.clone(), w0.zeros.clone(), w0.zero_bias,
+                                          K, N) for _ in range(copies - 1)]
+    xd = torch.from_numpy(x).cuda()
+    out = torch.empty((M, N), dtype=torch.float16, device="cuda")
+
+    def step():
+        for w in ws:
+            mcv.matmul_w4a16(xd, w, out)
+    s0 = torch.cuda.Stream()
+    step()
+    torch.cuda.synchronize()
+    g = graph_of(torch, step, s0)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    ms = time_graph_ms(torch, g, reps=20) / copies
+    us = ms * 1e3
+    gbs = per / (us * 1e-6) / 1e9
+    return {"config": "config0 M=1 K=1024 N=3584 group=128", "us_per_gemv": round(us, 4),
+            "GBps": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 4), "bytes_per_gemv": per,
+            "timing": f"CUDA graph of {copies} back-to-back GEMVs over distinct weight copies "
+                      f"({copies * w0.nbytes / 1e6:.0f} MB > 2x L2), PDL on, 20 replays",
+            "gpu_launches_per_replay": copies}
+
+
+def bench_w8a8(torch, mcv, synth, l2, hbm):
+    res = []
+    K = 1024
+    for M in (1, 4, 8):
+        for N in (1024, 3584):
+            x, w, wsc = synth.w8a8_inputs(M, K, N, seed=M * 10 + N)
+            wt = torch.from_numpy(np.ascontiguousarray(w.T)).cuda()
+            copies = max(2, int(np.ceil(2 * l2 / wt.numel())))
+            wts = [wt] + [wt.clone() for _ in range(copies - 1)]
+            xd = torch.from_numpy(x).cuda()
+            sd = torch.from_numpy(wsc).cuda()
+            out = torch.empty((M, N), dtype=torch.float16, device="cuda")
+
+            def step():
+                for t in wts:
+                    mcv.w8a8_fused(xd, t, sd, out, w_layout=0)
+            step()
+            torch.cuda.synchronize()
+            g = graph_of(torch, step, torch.cuda.Stream())
+            g.replay()
+            torch.cuda.synchronize()
+            us = time_graph_ms(torch, g, reps=10) / copies * 1e3
+            byts = K * N + N * 2 + M * K * 2 + M * N * 2
+            gbs = byts / (us * 1e-6) / 1e9
+            res.append({"M": M, "N": N, "us": round(us, 4), "GBps": round(gbs, 1),
+                        "frac_of_hbm": round(gbs / hbm, 4)})
+            del wts, g
+    return {"config": "config2 fused quantize+int8 GEMV+dequant, K=1024, weights [N][K]", "cases": res}
+
+
+def bench_decode_step(torch, mcv, synth, hbm, lm_w, ws_lm):
+    shapes = synth.decode_step_shapes()
+    weights = []
+    for i, (_, _, K, N) in enumerate(shapes):
+        _, q, z, s = synth.w4a16_inputs(1, K, N, seed=1000 + i)
+        weights.append(mcv.pack_w4a16(q, z, s))
+    xs = {K: torch.randn((1, K), device="cuda").to(torch.float16) for K in (1024, 2048, 3584)}
+    outs = {N: torch.empty((1, N), dtype=torch.float16, device="cuda") for _, _, _, N in shapes}
+    idx = torch.empty(1, dtype=torch.int64, device="cuda")
+    x_lm = xs[1024]
+
+    def step():
+        for (_, _, K, N), w in zip(shapes, weights):
+            mcv.matmul_w4a16(xs[K], w, outs[N])
+        mcv.lm_head_argmax(x_lm, lm_w, ws_lm, out_index=idx)
+    step()
+    torch.cuda.synchronize()
+    g = graph_of(torch, step, torch.cuda.Stream())
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    ms = time_graph_ms(torch, g, reps=10)
+    byts = sum(synth.w4a16_bytes(1, K, N) for _, _, K, N in shapes) + VOCAB * K_HIDDEN * 2 + K_HIDDEN * 2
+    gbs = byts / (ms * 1e-3) / 1e9
+    return {"config": "config3: 186 W4A16 GEMVs (24-layer hybrid LM) + fp16 lm_head argmax, M=1",
+            "us_per_token": round(ms * 1e3, 2), "bytes_per_token": byts, "GBps": round(gbs, 1),
+            "frac_of_hbm": round(gbs / hbm, 4), "gpu_launches_per_token": len(shapes) + 1,
+            "timing": "one CUDA graph per token (PDL edges), 10 replays"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="mcv", choices=["mcv", "reference"])
+    ap.add_argument("--no-extras", action="store_true", help="skip the config 0/2/3 sub-benchmarks")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import mcv_b200 as mcv
+    from mcv_b200 import synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    hbm, _tf, peak_kind = load_peaks()
+    props = torch.cuda.get_device_properties(local)
+    l2 = int(getattr(props, "L2_cache_size", 126 * 1024 * 1024))
+
+    # ---- shard of the vocabulary ----
+    per = (VOCAB + world - 1) // world
+    a, b = rank * per, min(VOCAB, (rank + 1) * per)
+    rows = b - a
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1234 + rank)
+    shard_bytes = rows * K_HIDDEN * 2
+    copies = max(1, int(np.ceil(2 * l2 / shard_bytes)))
+    w_copies = [rand_f16(torch, (rows, K_HIDDEN), 0.02, gen)]
+    w_copies += [w_copies[0].clone() for _ in range(copies - 1)]
+    x = rand_f16(torch, (1, K_HIDDEN), 1.0, gen)
+    if world > 1:
+        dist.broadcast(x, 0)
+    ws = mcv.lm_head_workspace(1)
+    key = torch.empty(1, dtype=torch.int64, device="cuda")
+    idx = torch.empty(1, dtype=torch.int64, device="cuda")
+    comm = None
+    if world > 1:
+        uid = [mcv.NcclComm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, 0)
+        comm = mcv.NcclComm(world, rank, uid[0])
+
+    def one_step(i):
+        w = w_copies[i % copies]
+        if comm is None:
+            mcv.lm_head_argmax(x, w, ws, out_index=idx, out_key=key)
+        else:
+            mcv.lm_head_argmax_allreduce(comm, x, w, ws, key, idx, n_offset=a)
+
+    def kernel_only(i):
+        mcv.lm_head_argmax(x, w_copies[i % copies], ws, out_key=key, n_offset=a)
+
+    cap = torch.cuda.Stream()
+    one_step(0)
+    torch.cuda.synchronize()
+    g_warm = graph_of(torch, lambda: [one_step(i) for i in range(args.warmup)], cap)
+    g_main = graph_of(torch, lambda: [one_step(i) for i in range(args.steps)], cap)
+    g_kern = graph_of(torch, lambda: [kernel_only(i) for i in range(args.steps)], cap)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    # untimed load so clocks settle and the sampler sees the loaded state
+    t_end = time.time() + 1.0
+    while time.time() < t_end:
+        g_warm.replay()
+        torch.cuda.synchronize()
+    g_warm.replay()
+    barrier()
+    ms_main = time_graph_ms(torch, g_main)
+    barrier()
+    ms_kern = time_graph_ms(torch, g_kern)
+    barrier()
+    clocks = sampler.stop() if sampler else None
+
+    # ---- end to end through the public API with host buffers ----
+    x_host = torch.empty((1, K_HIDDEN), dtype=torch.float16).pin_memory()
+    x_host.copy_(x.cpu())
+    idx_host = torch.empty(1, dtype=torch.int64).pin_memory()
+    x_dev = torch.empty_like(x)
+    e2e_steps = min(args.steps, 100)
+    s = torch.cuda.current_stream()
+
+    def e2e_step(i):
+        x_dev.copy_(x_host, non_blocking=True)
+        w = w_copies[i % copies]
+        if comm is None:
+            mcv.lm_head_argmax(x_dev, w, ws, out_index=idx)
+        else:
+            mcv.lm_head_argmax_allreduce(comm, x_dev, w, ws, key, idx, n_offset=a)
+        idx_host.copy_(idx, non_blocking=True)
+        s.synchronize()
+    for i in range(3):
+        e2e_step(i)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e1.record(s)
+    e1.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / e2e_steps
+
+    vals = torch.tensor([ms_main, ms_kern, ms_e2e], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms_main, ms_kern, ms_e2e = (float(v) for v in vals.cpu())
+    us_step = ms_main / args.steps * 1e3
+    us_kern = ms_kern / args.steps * 1e3
+
+    extras = {}
+    cpu_baseline = None
+    if rank == 0 and world == 1:
+        # CPU baseline: the oracle (a C port of the reference's CPU checker) on this host's cores
+        import oracle
+        nthreads = os.cpu_count() or 1
+        xh = x.cpu().numpy()
+        wh = w_copies[0].cpu().numpy()
+        oracle.lm_head_argmax(xh, wh, nthreads=nthreads)
+        reps = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            ci, _, _ = oracle.lm_head_argmax(xh, wh, nthreads=nthreads)
+            reps.append(time.perf_counter() - t0)
+        cpu_us = statistics.median(reps) * 1e6
+        cpu_baseline = {"value": round(cpu_us, 1), "unit": "us", "cores": nthreads, "kind": "port",
+                        "sample": "the full 248094-row lm_head + argmax of this run's weights, median of 3, "
+                                  "fp32 ascending-k dots (tests/test_lm_head_pipeline.cpp:95-107) "
+                                  f"split over {nthreads} threads"}
+        mcv.lm_head_argmax(x, w_copies[0], ws, out_index=idx)
+        extras["parity_check"] = {"gpu_index": int(idx.item()), "cpu_index": int(ci[0]),
+                                  "match": int(idx.item()) == int(ci[0])}
+        del wh
+        if not args.no_extras:
+            extras["w4a16_gemv"] = bench_w4a16_gemv(torch, mcv, synth, l2, hbm)
+            extras["w8a8"] = bench_w8a8(torch, mcv, synth, l2, hbm)
+            extras["decode_step"] = bench_decode_step(torch, mcv, synth, hbm, w_copies[0], ws)
+
+    if rank == 0:
+        algo_bytes = rows * K_HIDDEN * 2 + K_HIDDEN * 2 + 8
+        achieved = algo_bytes / (us_kern * 1e-6) / 1e9
+        traffic = load_traffic().get("lm_head_rows")
+        tr = None
+        if traffic:
+            tr = int(traffic["dram_bytes_per_row"] * rows + traffic.get("dram_bytes_fixed", 0))
+        line = {
+            "metric": METRIC, "value": round(us_step, 3), "unit": "us", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(us_step / 1e3, 6), "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded N(0,0.02) weights)",
+            "config": {"workload": WORKLOAD, "K": K_HIDDEN, "vocab": VOCAB, "M": 1, "shard_rows": rows,
+                       "parallelism": f"vocab-shard x{world}" + (" + NCCL allreduce(max) of uint64 key" if world > 1 else ""),
+                       "l2": f"inputs larger than L2: {copies} rotating copies of the {shard_bytes / 1e6:.1f} MB shard",
+                       "timing": "K steps in one CUDA graph, CUDA events, max over ranks"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "traffic": tr, "peak_kind": peak_kind,
+                         "kernel": "rows_kernel<argmax> (lm_head GEMV + argmax)",
+                         "kernel_us": round(us_kern, 3), "algorithmic_bytes": algo_bytes},
+            "cpu_baseline": cpu_baseline,
+            "e2e": {"value": round(ms_e2e * 1e3, 3), "unit": "us", "h2d_bytes_per_step": K_HIDDEN * 2,
+                    "d2h_bytes_per_step": 8,
+                    "note": "pinned x H2D + C-ABI call + index D2H + stream sync per step"},
+            "clocks": clocks,
+            "gpu_launches": args.steps * (1 if world == 1 else 2),
+        }
+        line.update(extras)
+        print(json.dumps(line), flush=True)
+    if comm is not None:
+        torch.cuda.synchronize()
+        comm.destroy()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

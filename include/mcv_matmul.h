@@ -1,0 +1,225 @@
+/*
+ * mcv_matmul.h -- C ABI of the B200 (sm_100a) decode-matmul library
+ * (libmcv_b200.so).
+ *
+ * This is the drop-in boundary for the decode matmul hot path of the
+ * MiniCPM-V 4.6 engine (lvyufeng/minicpm-v-4.6-orangepi).  Each entry point
+ * names the reference interface it replaces (file:line in that project).
+ *
+ * Conventions
+ *  - All tensor arguments are raw DEVICE pointers unless the name ends in
+ *    `_host`.  fp16 data is IEEE binary16 passed as `void*`/`uint16_t*`.
+ *  - Nothing here allocates device memory.  Buffers, including workspaces
+ *    sized by the `*_workspace_size` queries, belong to the caller.
+ *  - Calls are asynchronous and stream-ordered on `stream` (a cudaStream_t;
+ *    NULL = legacy default stream).  Unlike the reference, which synchronises
+ *    its stream after every op (src/csrc/lib/ops.cpp:359-377), no call here
+ *    synchronises; the C++ wrappers in mcv_ops.hpp offer that as an option.
+ *  - Every function returns an mcv_status; 0 is success.  Errors are reported,
+ *    never thrown and never trapped on the device; mcv_last_error() gives a
+ *    message for the calling thread.
+ *  - Kernels are launched with programmatic dependent launch: a GEMV issues
+ *    its weight loads before waiting for the previous kernel on the stream,
+ *    and reads activations only after that wait.  Weights must therefore not
+ *    be written by the kernel immediately preceding the call on the same
+ *    stream while that kernel is still running; use mcv_set_pdl(0) to turn
+ *    the early start off.
+ */
+#ifndef MCV_MATMUL_H
+#define MCV_MATMUL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* mcv_stream_t; /* cudaStream_t */
+
+enum mcv_status {
+    MCV_OK = 0,
+    MCV_ERR_NULL = 1,        /* a required pointer is NULL */
+    MCV_ERR_SHAPE = 2,       /* unsupported or inconsistent dimensions */
+    MCV_ERR_ALIGN = 3,       /* a pointer is not 16-byte aligned */
+    MCV_ERR_CUDA = 4,        /* a CUDA runtime call failed */
+    MCV_ERR_NCCL = 5,        /* an NCCL call failed */
+    MCV_ERR_WORKSPACE = 6,   /* workspace missing or too small */
+    MCV_ERR_VALUE = 7,       /* bad argument value (layout code, g_idx, zero range) */
+    MCV_ERR_TIMEOUT = 8      /* a bounded device-side wait gave up */
+};
+
+const char* mcv_status_string(int status);
+/* Message describing the last failure on the calling thread ("" if none). */
+const char* mcv_last_error(void);
+/* Library ABI version, (major << 16) | minor. */
+int mcv_version(void);
+/* 1 (default): launch kernels with programmatic dependent launch; 0: plain launches. */
+void mcv_set_pdl(int enabled);
+
+/* ======================================================================== */
+/* W4A16: int4 weights, fp16 group scales and 4-bit zeros, fp16 activations */
+/* ======================================================================== */
+/*
+ * Device weight layout "mcv-int4" (prepared once at load time):
+ *   qweight  uint32 [N][K/8]    column n's K values, 8 per word.  Within a
+ *                               word holding k = 8j..8j+7, the 4-bit value of
+ *                               k = 8j+i sits at nibble slot {0,4,1,5,2,6,3,7}[i],
+ *                               so one LOP3 per pair yields two fp16 lanes.
+ *   scales   fp16   [N][G]      G = K/group, scale of (group g, column n)
+ *   zeros    uint32 [N][ceil(G/8)]  4-bit zero of (g, n) at nibble g%8 of
+ *                               word g/8; effective zero = nibble + zero_bias
+ *   zero_bias 0 for AWQ and synthetic weights, 1 for GPTQ (whose stored zero
+ *             is one less than the true zero, src/csrc/lib/quantized_weight.cpp:112)
+ * Dequantised weight w[k][n] = (q - zero) * scale.  Requires K % group == 0,
+ * group % 32 == 0, and 16-byte aligned qweight.
+ */
+
+/* Bytes of each array of the mcv-int4 layout. */
+int mcv_w4a16_layout_bytes(int64_t K, int64_t N, int64_t group, size_t* qweight_bytes,
+                           size_t* scales_bytes, size_t* zeros_bytes);
+
+/* Host repack from logical arrays: q uint8 [K][N] (0..15), z uint8 [G][N]
+ * (0..15), scales fp16 [G][N].  Writes the three mcv-int4 arrays (host memory). */
+int mcv_w4a16_pack_host(const uint8_t* q_kn, const uint8_t* z_gn, const uint16_t* scales_gn,
+                        int64_t K, int64_t N, int64_t group, uint32_t* qweight_out,
+                        uint16_t* scales_out, uint32_t* zeros_out);
+
+/* Host repack of a GPTQ checkpoint tensor set (qweight int32 [K/8][N],
+ * qzeros int32 [G][N/8], g_idx int32 [K] or NULL, scales fp16 [G][N]).
+ * Replaces unpack_gptq_weight + pack_w4a16_weight of
+ * src/csrc/lib/quantized_weight.cpp:75-120, 48-73 (load_w4a16_quantized_weight,
+ * :212-229).  Like the reference kernel, scales are indexed by k/group, so a
+ * g_idx other than k/group is rejected (MCV_ERR_VALUE).  *zero_bias_out = 1. */
+int mcv_w4a16_pack_gptq_host(const int32_t* qweight, const int32_t* qzeros,
+                             const int32_t* g_idx, const uint16_t* scales, int64_t K,
+                             int64_t N, int64_t group, uint32_t* qweight_out,
+                             uint16_t* scales_out, uint32_t* zeros_out, int* zero_bias_out);
+
+/* Host repack of an AWQ tensor set (qweight int32 [K][N/8], qzeros int32
+ * [G][N/8], slot order {0,2,4,6,1,3,5,7}; scales fp16 [G][N]).
+ * Replaces unpack_awq_weight, src/csrc/lib/quantized_weight.cpp:122-160. */
+int mcv_w4a16_pack_awq_host(const int32_t* qweight, const int32_t* qzeros,
+                            const uint16_t* scales, int64_t K, int64_t N, int64_t group,
+                            uint32_t* qweight_out, uint16_t* scales_out, uint32_t* zeros_out,
+                            int* zero_bias_out);
+
+/* Host repack of the reference's own tile-packed int8 (q - zero) layout
+ * (src/csrc/lib/quantized_weight.cpp:41-73, the `w_int8` argument of
+ * matmul_w4a16, src/csrc/include/minicpmv/ops.h:95-108) with its scales fp16
+ * [G][N].  A zero is chosen per (group, column) so every value fits 4 bits;
+ * MCV_ERR_VALUE if a group/column spans more than 16 levels. */
+int mcv_w4a16_pack_from_tiles_host(const int8_t* packed, int64_t tile_len,
+                                   const uint16_t* scales_gn, int64_t K, int64_t N,
+                                   uint32_t* qweight_out, uint16_t* scales_out,
+                                   uint32_t* zeros_out, int* zero_bias_out);
+
+/* out[m][n] = sum_k x[m][k] * w[k][n], M = 1..8, fp32 accumulation, fp16 out.
+ * x fp16 [M][K], out fp16 [M][N].
+ * Replaces matmul_w4a16 (src/csrc/lib/ops.cpp:1030-1095, ops.h:95-108; M=1
+ * there) and its kernel op_kernel/matmul_w4a16_custom.cpp. */
+int mcv_w4a16_gemv(const void* x, const void* qweight, const void* scales, const void* zeros,
+                   int zero_bias, void* out, int64_t M, int64_t K, int64_t N, int64_t group,
+                   mcv_stream_t stream);
+
+/* ======================================================================== */
+/* dense fp16 GEMV and the lm_head                                          */
+/* ======================================================================== */
+
+/* out fp16 [M][N] = x fp16 [M][K] . W, M = 1..8, fp32 accumulation.
+ * w_layout 0: W stored [N][K] (the checkpoint / tied-embedding layout);
+ * w_layout 1: W stored [K][N] (the reference's pre-transposed "natural" B).
+ * Replaces matmul_b_transposed at M=1 (src/csrc/lib/ops.cpp:159-209,
+ * ops.h:19) and the cube kernel op_kernel/matmul_cube_custom.cpp. */
+int mcv_gemv_f16(const void* x, const void* w, void* out, int64_t M, int64_t K, int64_t N,
+                 int w_layout, mcv_stream_t stream);
+
+/* Workspace bytes for mcv_lm_head_argmax with M rows; must be zero-filled
+ * once before first use (each call leaves it zeroed again). */
+size_t mcv_lm_head_workspace_size(int64_t M);
+
+/* Fused lm_head GEMV + greedy argmax over one contiguous vocab shard.
+ *   x       fp16 [M][K] (M = 1..8)
+ *   w       fp16 [N_shard][K] rows of the tied embedding, global rows
+ *           n_offset .. n_offset+N_shard-1
+ *   out_key uint64 [M] (may be NULL): order-preserving argmax key,
+ *           (ordered fp32 bits of the winning logit << 32) | (0xFFFFFFFF - index)
+ *   out_index int64 [M] (may be NULL): winning global vocab index
+ * Logits are fp32 dots; ties go to the smallest index (the first maximum,
+ * language_model.cpp:475 and tests/test_lm_head_pipeline.cpp:104).
+ * fp16_logits = 1 compares logits rounded to fp16, as the production
+ * lm_head_greedy does on its D2H-copied fp16 chunk (language_model.cpp:471-479).
+ * Replaces the per-chunk matmul + D2H + host argmax loop of lm_head_greedy,
+ * src/csrc/lib/language_model.cpp:464-480. */
+int mcv_lm_head_argmax(const void* x, const void* w, void* out_key, void* out_index, int64_t M,
+                       int64_t K, int64_t N_shard, int64_t n_offset, int fp16_logits,
+                       void* workspace, size_t workspace_bytes, mcv_stream_t stream);
+
+/* Greedy argmax of fp16 logits [M][V] -> int64 [M], first maximum wins.
+ * Replaces argmax_last_dim (src/csrc/lib/ops.cpp:324-357, ops.h:21). */
+int mcv_argmax_last_dim_f16(const void* logits, void* out_index, int64_t M, int64_t V,
+                            mcv_stream_t stream);
+
+/* int64 index[m] = 0xFFFFFFFF - (uint32)key[m]: decode argmax keys on the device. */
+int mcv_argmax_key_to_index(const void* key, void* out_index, int64_t M, mcv_stream_t stream);
+
+/* ---- sharded lm_head across GPUs (one process per GPU, NCCL over NVLink) -- */
+/* Size of an NCCL unique id (bytes). */
+size_t mcv_nccl_unique_id_bytes(void);
+/* Rank 0 creates the id; the caller distributes it to every rank. */
+int mcv_nccl_get_unique_id(void* id_out);
+/* Creates this rank's communicator on the current CUDA device. */
+int mcv_nccl_comm_init(void** comm_out, int nranks, const void* id, int rank);
+int mcv_nccl_comm_destroy(void* comm);
+/* mcv_lm_head_argmax on this rank's shard, then one ncclAllReduce(max) of the
+ * M uint64 keys, then the index decode: every rank ends with the global
+ * argmax in out_index (int64 [M]) and out_key (uint64 [M], required). */
+int mcv_lm_head_argmax_allreduce(void* comm, const void* x, const void* w, void* out_key,
+                                 void* out_index, int64_t M, int64_t K, int64_t N_shard,
+                                 int64_t n_offset, int fp16_logits, void* workspace,
+                                 size_t workspace_bytes, mcv_stream_t stream);
+
+/* ======================================================================== */
+/* W8A8: int8 activations (per-token absmax) x int8 weights (per channel)   */
+/* ======================================================================== */
+
+/* Per-row symmetric absmax quantization of x fp16 [M][K] to int8 [M][K] and
+ * fp16 scales [M]: scale = max|x|/127 (>= 1e-8), q = trunc(clamp(x/scale) +/- 0.5).
+ * Replaces w8a8_quantize (src/csrc/lib/ops.cpp:1135-1171, kernel
+ * op_kernel/w8a8_quantize_custom.cpp:25-41; M=1 there). */
+int mcv_w8a8_quantize(const void* x, void* x_int8, void* x_scale, int64_t M, int64_t K,
+                      mcv_stream_t stream);
+
+/* int32 acc [M][N] = x_int8 [M][K] . w_int8, bit-exact.  w_layout 0: w [N][K]
+ * (this library's fast layout), 1: w [K][N] (the reference's layout).
+ * Replaces matmul_w8a8_i32 (src/csrc/lib/ops.cpp:1097-1133,
+ * op_kernel/matmul_w8a8_i32_custom.cpp). */
+int mcv_w8a8_gemm_i32(const void* x_int8, const void* w_int8, void* acc, int64_t M, int64_t K,
+                      int64_t N, int w_layout, mcv_stream_t stream);
+
+/* out fp16 [M][N] = fp16_rn((float(acc) * float(w_scale[n])) * float(x_scale[m])).
+ * Replaces w8a8_dequant (src/csrc/lib/ops.cpp:1173-1210,
+ * op_kernel/w8a8_dequant_custom.cpp:52-59). */
+int mcv_w8a8_dequant(const void* acc, const void* x_scale, const void* w_scale, void* out,
+                     int64_t M, int64_t N, mcv_stream_t stream);
+
+/* Quantize + int8 GEMM + dequant in one kernel (w_layout 0) or three
+ * (w_layout 1).  acc_out (int32 [M][N]), x_int8_out and x_scale_out are
+ * optional copies of the intermediates (may be NULL).
+ * Replaces the W8A8 branch of matmul_decode_dispatch
+ * (src/csrc/lib/decoder_layer.cpp:216-232). */
+int mcv_w8a8_fused(const void* x, const void* w_int8, const void* w_scale, void* out,
+                   void* acc_out, void* x_int8_out, void* x_scale_out, int64_t M, int64_t K,
+                   int64_t N, int w_layout, mcv_stream_t stream);
+
+/* Per-output-channel int8 quantization of an fp16 weight stored [K][N]:
+ * w_scale fp16 [N] (truncating fp16 conversion, as the reference), wq int8 in
+ * w_layout 0 ([N][K]) or 1 ([K][N]).
+ * Replaces quantize_dense_weight_w8a8 (src/csrc/lib/quantized_weight.cpp:231-268). */
+int mcv_w8a8_quantize_weight(const void* w_kn, void* wq, void* w_scale, int64_t K, int64_t N,
+                             int w_layout, mcv_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

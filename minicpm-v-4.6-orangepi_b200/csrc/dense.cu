@@ -1,0 +1,423 @@
+// Dense fp16 decode GEMV (M = 1..8) in both weight layouts, the fused
+// lm_head GEMV + greedy argmax, and argmax over fp16 logits.
+//
+// Reference behaviour replaced:
+//  * matmul_b_transposed at M=1 (src/csrc/lib/ops.cpp:159-209) and its cube
+//    kernel (op_kernel/matmul_cube_custom.cpp:19-55);
+//  * lm_head_greedy's 16 sequential [1024,16384] chunk matmuls, each followed
+//    by a D2H copy of fp16 logits and a host argmax with strict '>'
+//    (src/csrc/lib/language_model.cpp:412-482);
+//  * argmax_last_dim (src/csrc/lib/ops.cpp:324-357).
+//
+// Row kernel ([N][K] weights, K contiguous): one warp per weight row, lane l
+// reads 16-byte chunks l, l+32, ... of the row (512 contiguous bytes per
+// warp-wide load), fp16 x fp16 products accumulate in fp32 with the sm_100
+// mixed-precision FMA, and a 5-step xor-shuffle finishes the dot.  The grid
+// is persistent (a multiple of the SM count) and walks rows with a stride, two
+// rows per warp per step.  In argmax mode each logit becomes a 64-bit
+// order-preserving key (larger logit wins, then smaller index) so the whole
+// reduction is an integer max: per warp in registers, per block in shared
+// memory, and across blocks by the last block to finish (a counter in the
+// caller's workspace, reset by that block so the next call needs no memset).
+#include "common.cuh"
+
+namespace mcv {
+namespace {
+
+constexpr int kRowThreads = 256;
+constexpr int kRowWarps = kRowThreads / 32;
+constexpr int kRowsPerStep = 2;
+
+struct RowArgs {
+    const __half* x;
+    const __half* w;
+    __half* out;            // GEMV mode
+    uint64_t* partial;      // argmax: [gridDim.x][M]
+    unsigned* counter;      // argmax: blocks finished
+    uint64_t* out_key;      // argmax: [M] (may be null)
+    int64_t* out_index;     // argmax: [M] (may be null)
+    int64_t N;
+    int K;
+    int64_t n_offset;
+};
+
+template <int M, int KCH, bool ARGMAX, bool FP16_LOGITS>
+__global__ void __launch_bounds__(kRowThreads)
+rows_kernel(RowArgs a) {
+    extern __shared__ uint4 xs[];  // x as [M][K/8] 16-byte chunks
+    __shared__ uint64_t red[kRowWarps][M];
+    __shared__ int is_last;
+
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int chunks = a.K >> 3;
+    const int64_t gwarp = static_cast<int64_t>(blockIdx.x) * kRowWarps + warp;
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kRowWarps;
+    const uint4* w4 = reinterpret_cast<const uint4*>(a.w);
+
+    // Prefetch this warp's first rows before waiting on the previous kernel.
+    uint4 wv[kRowsPerStep][KCH];
+    int64_t r = gwarp * kRowsPerStep;
+    const int64_t step = nwarps * kRowsPerStep;
+#pragma unroll
+    for (int t = 0; t < kRowsPerStep; ++t)
+#pragma unroll
+        for (int i = 0; i < KCH; ++i) {
+            const int c = lane + 32 * i;
+            if (r + t < a.N && c < chunks) wv[t][i] = ld_stream(w4 + (r + t) * chunks + c);
+        }
+    pdl_trigger();
+    pdl_wait();
+    for (int idx = threadIdx.x; idx < M * chunks; idx += kRowThreads)
+        xs[idx] = reinterpret_cast<const uint4*>(a.x)[idx];
+    __syncthreads();
+
+    uint64_t best[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) best[m] = 0;
+
+    while (r < a.N) {
+        float acc0[kRowsPerStep][M], acc1[kRowsPerStep][M];
+#pragma unroll
+        for (int t = 0; t < kRowsPerStep; ++t)
+#pragma unroll
+            for (int m = 0; m < M; ++m) acc0[t][m] = acc1[t][m] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < KCH; ++i) {
+            const int c = lane + 32 * i;
+            if (c < chunks) {
+#pragma unroll
+                for (int m = 0; m < M; ++m) {
+                    const uint4 xv = xs[m * chunks + c];
+#pragma unroll
+                    for (int t = 0; t < kRowsPerStep; ++t) {
+                        fma2_f16_f32(acc0[t][m], acc1[t][m], wv[t][i].x, xv.x);
+                        fma2_f16_f32(acc0[t][m], acc1[t][m], wv[t][i].y, xv.y);
+                        fma2_f16_f32(acc0[t][m], acc1[t][m], wv[t][i].z, xv.z);
+                        fma2_f16_f32(acc0[t][m], acc1[t][m], wv[t][i].w, xv.w);
+                    }
+                }
+            }
+        }
+        // issue the next step's loads before reducing this one
+        const int64_t rn = r + step;
+#pragma unroll
+        for (int t = 0; t < kRowsPerStep; ++t)
+#pragma unroll
+            for (int i = 0; i < KCH; ++i) {
+                const int c = lane + 32 * i;
+                if (rn + t < a.N && c < chunks) wv[t][i] = ld_stream(w4 + (rn + t) * chunks + c);
+            }
+#pragma unroll
+        for (int t = 0; t < kRowsPerStep; ++t) {
+            const int64_t row = r + t;
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                float v = warp_sum(acc0[t][m] + acc1[t][m]);
+                if (row < a.N) {
+                    if constexpr (ARGMAX) {
+                        if constexpr (FP16_LOGITS) v = __half2float(__float2half_rn(v));
+                        const uint64_t key = argmax_key(v, static_cast<uint32_t>(a.n_offset + row));
+                        best[m] = key > best[m] ? key : best[m];
+                    } else {
+                        if (lane == m) a.out[static_cast<int64_t>(m) * a.N + row] = __float2half_rn(v);
+                    }
+                }
+            }
+        }
+        r = rn;
+    }
+
+    if constexpr (ARGMAX) {
+        // keys are already warp-uniform (butterfly reduction)
+        if (lane == 0) {
+#pragma unroll
+            for (int m = 0; m < M; ++m) red[warp][m] = best[m];
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                uint64_t b = 0;
+                for (int wi = 0; wi < kRowWarps; ++wi) b = red[wi][m] > b ? red[wi][m] : b;
+                a.partial[static_cast<int64_t>(blockIdx.x) * M + m] = b;
+            }
+            __threadfence();
+            const unsigned prev = atomicAdd(a.counter, 1u);
+            is_last = (prev == gridDim.x - 1);
+        }
+        __syncthreads();
+        if (is_last) {
+            __threadfence();
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                uint64_t b = 0;
+                for (int blk = threadIdx.x; blk < static_cast<int>(gridDim.x); blk += kRowThreads) {
+                    const uint64_t v = __ldcg(a.partial + static_cast<int64_t>(blk) * M + m);
+                    b = v > b ? v : b;
+                }
+                b = warp_max_u64(b);
+                if (lane == 0) red[warp][m] = b;
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) {
+#pragma unroll
+                for (int m = 0; m < M; ++m) {
+                    uint64_t b = 0;
+                    for (int wi = 0; wi < kRowWarps; ++wi) b = red[wi][m] > b ? red[wi][m] : b;
+                    if (a.out_key) a.out_key[m] = b;
+                    if (a.out_index)
+                        a.out_index[m] = static_cast<int64_t>(0xffffffffu - static_cast<uint32_t>(b & 0xffffffffu));
+                }
+                *a.counter = 0u;  // leave the workspace ready for the next call
+            }
+        }
+    }
+}
+
+// [K][N] natural layout: each thread owns 8 consecutive columns (one 16-byte
+// load per k row); 4 threads span 32 columns, 64 threads split K; partial
+// sums meet in shared memory.
+constexpr int kKnTx = 4;
+constexpr int kKnTy = 64;
+
+template <int M>
+__global__ void __launch_bounds__(kKnTx * kKnTy)
+gemv_kn_kernel(const __half* __restrict__ x, const __half* __restrict__ w, __half* __restrict__ out,
+               int K, int N) {
+    extern __shared__ float red_kn[];  // [kKnTy][M][kKnTx*8]
+    const int tx = threadIdx.x % kKnTx;
+    const int ty = threadIdx.x / kKnTx;
+    const int n0 = blockIdx.x * (kKnTx * 8) + tx * 8;
+    pdl_trigger();
+    pdl_wait();
+    float acc[M][8];
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[m][e] = 0.0f;
+    if (n0 < N) {
+        for (int k = ty; k < K; k += kKnTy) {
+            const uint4 wv = ld_stream(w + static_cast<int64_t>(k) * N + n0);
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                const __half xh = x[static_cast<int64_t>(m) * K + k];
+                const uint32_t xx = h2_as_u32(__halves2half2(xh, xh));
+                fma2_f16_f32(acc[m][0], acc[m][1], wv.x, xx);
+                fma2_f16_f32(acc[m][2], acc[m][3], wv.y, xx);
+                fma2_f16_f32(acc[m][4], acc[m][5], wv.z, xx);
+                fma2_f16_f32(acc[m][6], acc[m][7], wv.w, xx);
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) red_kn[(ty * M + m) * (kKnTx * 8) + tx * 8 + e] = acc[m][e];
+    __syncthreads();
+    for (int o = threadIdx.x; o < M * kKnTx * 8; o += kKnTx * kKnTy) {
+        const int m = o / (kKnTx * 8);
+        const int col = o % (kKnTx * 8);
+        float s = 0.0f;
+        for (int t = 0; t < kKnTy; ++t) s += red_kn[(t * M + m) * (kKnTx * 8) + col];
+        const int n = blockIdx.x * (kKnTx * 8) + col;
+        if (n < N) out[static_cast<int64_t>(m) * N + n] = __float2half_rn(s);
+    }
+}
+
+constexpr int kArgThreads = 512;
+
+__global__ void __launch_bounds__(kArgThreads)
+argmax_rows_kernel(const __half* __restrict__ logits, int64_t* __restrict__ out, int64_t V) {
+    __shared__ uint64_t red[kArgThreads / 32];
+    pdl_trigger();
+    pdl_wait();
+    const __half* row = logits + static_cast<int64_t>(blockIdx.x) * V;
+    uint64_t best = 0;
+    for (int64_t v = threadIdx.x; v < V; v += kArgThreads) {
+        const uint64_t k = argmax_key(__half2float(row[v]), static_cast<uint32_t>(v));
+        best = k > best ? k : best;
+    }
+    best = warp_max_u64(best);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint64_t b = 0;
+        for (int i = 0; i < kArgThreads / 32; ++i) b = red[i] > b ? red[i] : b;
+        out[blockIdx.x] = static_cast<int64_t>(0xffffffffu - static_cast<uint32_t>(b & 0xffffffffu));
+    }
+}
+
+__global__ void key_to_index_kernel(const uint64_t* __restrict__ key, int64_t* __restrict__ out, int M) {
+    pdl_trigger();
+    pdl_wait();
+    const int m = threadIdx.x;
+    if (m < M) out[m] = static_cast<int64_t>(0xffffffffu - static_cast<uint32_t>(key[m] & 0xffffffffu));
+}
+
+int row_grid(int64_t N) {
+    // persistent grid: up to 4 blocks of 256 threads per SM, never more
+    // blocks than there are row pairs to hand out
+    const int64_t warps_needed = (N + kRowsPerStep - 1) / kRowsPerStep;
+    const int64_t blocks_needed = (warps_needed + kRowWarps - 1) / kRowWarps;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 4;
+    return static_cast<int>(blocks_needed < cap ? blocks_needed : cap);
+}
+
+template <int M, bool ARGMAX, bool FP16>
+int launch_rows_m(int kch, const RowArgs& a, cudaStream_t s, int grid) {
+    const size_t smem = static_cast<size_t>(M) * a.K * 2;
+    auto pick = [&](auto kern) -> int {
+        if (smem > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(smem));
+            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rows_kernel)");
+        }
+        return launch(kern, dim3(grid), dim3(kRowThreads), smem, s, a);
+    };
+    switch (kch) {
+        case 1: return pick(rows_kernel<M, 1, ARGMAX, FP16>);
+        case 2: return pick(rows_kernel<M, 2, ARGMAX, FP16>);
+        case 4: return pick(rows_kernel<M, 4, ARGMAX, FP16>);
+        case 8: return pick(rows_kernel<M, 8, ARGMAX, FP16>);
+        default: return fail(MCV_ERR_SHAPE, "row kernel: K above 16384 unsupported");
+    }
+}
+
+template <bool ARGMAX, bool FP16>
+int launch_rows(int64_t M, const RowArgs& a, cudaStream_t s, int grid) {
+    const int chunks_per_lane = (a.K / 8 + 31) / 32;
+    int kch = 1;
+    while (kch < chunks_per_lane) kch *= 2;
+    switch (M) {
+        case 1: return launch_rows_m<1, ARGMAX, FP16>(kch, a, s, grid);
+        case 2: return launch_rows_m<2, ARGMAX, FP16>(kch, a, s, grid);
+        case 3: return launch_rows_m<3, ARGMAX, FP16>(kch, a, s, grid);
+        case 4: return launch_rows_m<4, ARGMAX, FP16>(kch, a, s, grid);
+        case 5: return launch_rows_m<5, ARGMAX, FP16>(kch, a, s, grid);
+        case 6: return launch_rows_m<6, ARGMAX, FP16>(kch, a, s, grid);
+        case 7: return launch_rows_m<7, ARGMAX, FP16>(kch, a, s, grid);
+        default: return launch_rows_m<8, ARGMAX, FP16>(kch, a, s, grid);
+    }
+}
+
+int check_rows(const void* x, const void* w, int64_t M, int64_t K, int64_t N) {
+    if (!x || !w) return fail(MCV_ERR_NULL, "null x or w");
+    if (M < 1 || M > 8) return fail(MCV_ERR_SHAPE, "M must be 1..8");
+    if (K <= 0 || N <= 0 || K % 8 != 0) return fail(MCV_ERR_SHAPE, "K must be a positive multiple of 8 and N positive");
+    if (K > 16384) return fail(MCV_ERR_SHAPE, "K above 16384 unsupported");
+    if (!aligned16(x) || !aligned16(w)) return fail(MCV_ERR_ALIGN, "x and w must be 16-byte aligned");
+    return MCV_OK;
+}
+
+}  // namespace
+
+// Used by the collective entry point in collective.cu.
+int lm_head_argmax_impl(const void* x, const void* w, void* out_key, void* out_index, int64_t M,
+                        int64_t K, int64_t N, int64_t n_offset, int fp16_logits, void* ws,
+                        size_t ws_bytes, cudaStream_t s) {
+    int st = check_rows(x, w, M, K, N);
+    if (st) return st;
+    if (n_offset < 0 || n_offset + N > 0xffffffffLL) return fail(MCV_ERR_SHAPE, "lm_head: global vocab index must fit 32 bits");
+    if (!ws) return fail(MCV_ERR_WORKSPACE, "lm_head: workspace is null");
+    if (ws_bytes < mcv_lm_head_workspace_size(M)) return fail(MCV_ERR_WORKSPACE, "lm_head: workspace too small");
+    if (reinterpret_cast<uintptr_t>(ws) & 7u) return fail(MCV_ERR_ALIGN, "lm_head: workspace must be 8-byte aligned");
+    const int grid = row_grid(N);
+    RowArgs a{};
+    a.x = static_cast<const __half*>(x);
+    a.w = static_cast<const __half*>(w);
+    a.counter = static_cast<unsigned*>(ws);
+    a.partial = reinterpret_cast<uint64_t*>(static_cast<char*>(ws) + 256);
+    a.out_key = static_cast<uint64_t*>(out_key);
+    a.out_index = static_cast<int64_t*>(out_index);
+    a.N = N;
+    a.K = static_cast<int>(K);
+    a.n_offset = n_offset;
+    return fp16_logits ? launch_rows<true, true>(M, a, s, grid) : launch_rows<true, false>(M, a, s, grid);
+}
+
+int key_to_index_impl(const void* key, void* out_index, int64_t M, cudaStream_t s) {
+    return launch(key_to_index_kernel, dim3(1), dim3(32), 0, s, static_cast<const uint64_t*>(key),
+                  static_cast<int64_t*>(out_index), static_cast<int>(M));
+}
+
+}  // namespace mcv
+
+using namespace mcv;
+
+extern "C" {
+
+int mcv_gemv_f16(const void* x, const void* w, void* out, int64_t M, int64_t K, int64_t N, int w_layout,
+                 mcv_stream_t stream) {
+    int st = check_rows(x, w, M, K, N);
+    if (st) return st;
+    if (!out) return fail(MCV_ERR_NULL, "gemv_f16: null out");
+    auto s = static_cast<cudaStream_t>(stream);
+    if (w_layout == 0) {
+        if (N > 0x7fffffffLL) return fail(MCV_ERR_SHAPE, "gemv_f16: N too large");
+        RowArgs a{};
+        a.x = static_cast<const __half*>(x);
+        a.w = static_cast<const __half*>(w);
+        a.out = static_cast<__half*>(out);
+        a.N = N;
+        a.K = static_cast<int>(K);
+        return launch_rows<false, false>(M, a, s, row_grid(N));
+    }
+    if (w_layout != 1) return fail(MCV_ERR_VALUE, "gemv_f16: w_layout must be 0 ([N][K]) or 1 ([K][N])");
+    if (N % 8 != 0) return fail(MCV_ERR_SHAPE, "gemv_f16: [K][N] layout needs N % 8 == 0");
+    const dim3 grid(static_cast<unsigned>((N + kKnTx * 8 - 1) / (kKnTx * 8)));
+    const dim3 block(kKnTx * kKnTy);
+    const size_t smem = static_cast<size_t>(kKnTy) * M * kKnTx * 8 * sizeof(float);
+    auto xs = static_cast<const __half*>(x);
+    auto ws = static_cast<const __half*>(w);
+    auto o = static_cast<__half*>(out);
+    const int k = static_cast<int>(K), n = static_cast<int>(N);
+    auto go = [&](auto kern) -> int {
+        if (smem > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv_kn)");
+        }
+        return launch(kern, grid, block, smem, s, xs, ws, o, k, n);
+    };
+    switch (M) {
+        case 1: return go(gemv_kn_kernel<1>);
+        case 2: return go(gemv_kn_kernel<2>);
+        case 3: return go(gemv_kn_kernel<3>);
+        case 4: return go(gemv_kn_kernel<4>);
+        case 5: return go(gemv_kn_kernel<5>);
+        case 6: return go(gemv_kn_kernel<6>);
+        case 7: return go(gemv_kn_kernel<7>);
+        default: return go(gemv_kn_kernel<8>);
+    }
+}
+
+size_t mcv_lm_head_workspace_size(int64_t M) {
+    if (M < 1) M = 1;
+    // 256 B header (the block counter) + one key per (block, row); the grid is
+    // at most 4 blocks per SM, sized here for parts with up to 1024 SMs.
+    return 256 + static_cast<size_t>(4 * 1024) * static_cast<size_t>(M) * sizeof(uint64_t);
+}
+
+int mcv_lm_head_argmax(const void* x, const void* w, void* out_key, void* out_index, int64_t M, int64_t K,
+                       int64_t N_shard, int64_t n_offset, int fp16_logits, void* workspace,
+                       size_t workspace_bytes, mcv_stream_t stream) {
+    if (!out_key && !out_index) return fail(MCV_ERR_NULL, "lm_head_argmax: out_key and out_index both null");
+    return lm_head_argmax_impl(x, w, out_key, out_index, M, K, N_shard, n_offset, fp16_logits, workspace,
+                               workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int mcv_argmax_last_dim_f16(const void* logits, void* out_index, int64_t M, int64_t V, mcv_stream_t stream) {
+    if (!logits || !out_index) return fail(MCV_ERR_NULL, "argmax_last_dim: null pointer");
+    if (M < 1 || M > 0x7fffffffLL || V < 1 || V > 0xffffffffLL) return fail(MCV_ERR_SHAPE, "argmax_last_dim: bad shape");
+    return launch(argmax_rows_kernel, dim3(static_cast<unsigned>(M)), dim3(kArgThreads), 0,
+                  static_cast<cudaStream_t>(stream), static_cast<const __half*>(logits),
+                  static_cast<int64_t*>(out_index), V);
+}
+
+int mcv_argmax_key_to_index(const void* key, void* out_index, int64_t M, mcv_stream_t stream) {
+    if (!key || !out_index) return fail(MCV_ERR_NULL, "argmax_key_to_index: null pointer");
+    if (M < 1 || M > 32) return fail(MCV_ERR_SHAPE, "argmax_key_to_index: M must be 1..32");
+    return key_to_index_impl(key, out_index, M, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

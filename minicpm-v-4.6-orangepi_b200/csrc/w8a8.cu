@@ -1,0 +1,485 @@
+// W8A8 decode path: per-token int8 activation quantization, int8 x int8 ->
+// int32 GEMV (bit-exact), per-channel x per-token dequant to fp16, and the
+// per-channel weight quantizer.
+//
+// Reference behaviour replaced (src/csrc/lib/ops.cpp:1097-1210 and the
+// AscendC kernels it launches):
+//  * w8a8_quantize  (op_kernel/w8a8_quantize_custom.cpp:25-41): scale =
+//    max|x|/127 in fp32, clamped to >= 1e-8, inv = 1/scale, q = (int)(clamp(
+//    x*inv, -128, 127) +/- 0.5), scale stored as fp16.  Done per row here.
+//  * matmul_w8a8_i32 (op_kernel/matmul_w8a8_i32_custom.cpp): exact int32.
+//  * w8a8_dequant   (op_kernel/w8a8_dequant_custom.cpp:52-59): fp16 RN of
+//    (float(acc) * float(w_scale)) * float(x_scale).
+//  * quantize_dense_weight_w8a8 (src/csrc/lib/quantized_weight.cpp:231-268).
+// Every floating-point step uses an explicitly rounded intrinsic
+// (__fdiv_rn, __fmul_rn, __fadd_rn, __float2half_rn) so results are
+// bit-identical to the fp32 C restatement of those formulas.
+//
+// Fast layout: weights int8 [N][K] (K contiguous).  One warp owns two output
+// columns; lane l loads 16-byte chunks (16 k) l, l+32, ...; DP4A multiplies
+// four int8 pairs per instruction; a 5-step shuffle sums the warp.  The fused
+// kernel quantizes x inside every block (x is a few KB in L2), prefetches its
+// weights before the PDL wait, and writes fp16 outputs directly.
+#include "common.cuh"
+
+namespace mcv {
+namespace {
+
+constexpr int kQThreads = 256;
+constexpr int kW8Warps = 8;
+constexpr int kW8Cpw = 2;
+
+__device__ __forceinline__ int8_t quant_act(float v, float inv) {
+    float q = __fmul_rn(v, inv);
+    q = q > 127.0f ? 127.0f : q;
+    q = q < -128.0f ? -128.0f : q;
+    q = q >= 0.0f ? __fadd_rn(q, 0.5f) : __fsub_rn(q, 0.5f);
+    return static_cast<int8_t>(__float2int_rz(q));
+}
+
+__device__ __forceinline__ float scale_from_absmax(float max_abs) {
+    float s = __fdiv_rn(max_abs, 127.0f);
+    return s < 0.00000001f ? 0.00000001f : s;
+}
+
+// Block-wide max of non-negative floats (bit pattern order == value order).
+__device__ __forceinline__ float block_max_nonneg(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float r = 0.0f;
+    for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) r = fmaxf(r, red[i]);
+    return r;
+}
+
+// ---- standalone per-row quantizer --------------------------------------------
+__global__ void __launch_bounds__(kQThreads)
+quantize_rows_kernel(const __half* __restrict__ x, int8_t* __restrict__ xq, __half* __restrict__ xs, int K) {
+    __shared__ float red[kQThreads / 32];
+    pdl_trigger();
+    pdl_wait();
+    const __half* row = x + static_cast<int64_t>(blockIdx.x) * K;
+    float m = 0.0f;
+    for (int i = threadIdx.x; i < K; i += kQThreads) m = fmaxf(m, fabsf(__half2float(row[i])));
+    const float max_abs = block_max_nonneg(m, red);
+    const float scale = scale_from_absmax(max_abs);
+    const float inv = __fdiv_rn(1.0f, scale);
+    for (int i = threadIdx.x; i < K; i += kQThreads)
+        xq[static_cast<int64_t>(blockIdx.x) * K + i] = quant_act(__half2float(row[i]), inv);
+    if (threadIdx.x == 0) xs[blockIdx.x] = __float2half_rn(scale);
+}
+
+// ---- int8 GEMV over [N][K] weights, optionally fused ----------------------------
+struct W8Args {
+    const void* x;          // FUSED: fp16 [M][K]; else int8 [M][K]
+    const int8_t* w;        // [N][K]
+    const __half* w_scale;  // [N] (FUSED)
+    __half* out;            // [M][N] (FUSED)
+    int32_t* acc;           // [M][N] (optional when FUSED)
+    int8_t* xq_out;         // [M][K] (optional, FUSED, written by block 0)
+    __half* xs_out;         // [M]    (optional, FUSED, written by block 0)
+    int K;
+    int N;
+};
+
+template <int M, int KCH, bool FUSED>
+__global__ void __launch_bounds__(kW8Warps * 32)
+w8_rows_kernel(W8Args a) {
+    extern __shared__ uint4 xq_s[];  // int8 x as [M][K/16] 16-byte chunks
+    __shared__ float red[kW8Warps];
+    __shared__ float xscale_s[M];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int n0 = (blockIdx.x * kW8Warps + warp) * kW8Cpw;
+    const int chunks = a.K >> 4;
+
+    uint4 wv[kW8Cpw][KCH];
+    float wsc[kW8Cpw];
+#pragma unroll
+    for (int j = 0; j < kW8Cpw; ++j) {
+        const int n = n0 + j;
+        wsc[j] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < KCH; ++i) {
+            const int c = lane + 32 * i;
+            wv[j][i] = make_uint4(0, 0, 0, 0);
+            if (n < a.N && c < chunks) wv[j][i] = ld_stream(a.w + static_cast<int64_t>(n) * a.K + c * 16);
+        }
+        if constexpr (FUSED) {
+            if (n < a.N) wsc[j] = __half2float(a.w_scale[n]);
+        }
+    }
+    pdl_trigger();
+    pdl_wait();
+
+    int8_t* xq8 = reinterpret_cast<int8_t*>(xq_s);
+    if constexpr (FUSED) {
+        const __half* xh = static_cast<const __half*>(a.x);
+#pragma unroll 1
+        for (int m = 0; m < M; ++m) {
+            float mx = 0.0f;
+            for (int i = threadIdx.x; i < a.K; i += kW8Warps * 32)
+                mx = fmaxf(mx, fabsf(__half2float(xh[static_cast<int64_t>(m) * a.K + i])));
+            const float scale = scale_from_absmax(block_max_nonneg(mx, red));
+            const float inv = __fdiv_rn(1.0f, scale);
+            for (int i = threadIdx.x; i < a.K; i += kW8Warps * 32) {
+                const int8_t q = quant_act(__half2float(xh[static_cast<int64_t>(m) * a.K + i]), inv);
+                xq8[m * a.K + i] = q;
+                if (blockIdx.x == 0 && a.xq_out) a.xq_out[static_cast<int64_t>(m) * a.K + i] = q;
+            }
+            if (threadIdx.x == 0) {
+                const __half sh = __float2half_rn(scale);
+                xscale_s[m] = __half2float(sh);
+                if (blockIdx.x == 0 && a.xs_out) a.xs_out[m] = sh;
+            }
+        }
+    } else {
+        const uint4* src = static_cast<const uint4*>(a.x);
+        for (int idx = threadIdx.x; idx < M * chunks; idx += kW8Warps * 32) xq_s[idx] = src[idx];
+    }
+    __syncthreads();
+
+    int acc[kW8Cpw][M];
+#pragma unroll
+    for (int j = 0; j < kW8Cpw; ++j)
+#pragma unroll
+        for (int m = 0; m < M; ++m) acc[j][m] = 0;
+#pragma unroll
+    for (int i = 0; i < KCH; ++i) {
+        const int c = lane + 32 * i;
+        if (c < chunks) {
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                const uint4 xv = xq_s[m * chunks + c];
+#pragma unroll
+                for (int j = 0; j < kW8Cpw; ++j) {
+                    int s = acc[j][m];
+                    s = __dp4a(static_cast<int>(wv[j][i].x), static_cast<int>(xv.x), s);
+                    s = __dp4a(static_cast<int>(wv[j][i].y), static_cast<int>(xv.y), s);
+                    s = __dp4a(static_cast<int>(wv[j][i].z), static_cast<int>(xv.z), s);
+                    s = __dp4a(static_cast<int>(wv[j][i].w), static_cast<int>(xv.w), s);
+                    acc[j][m] = s;
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kW8Cpw; ++j)
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            int v = acc[j][m];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            const int n = n0 + j;
+            if (lane == ((j * M + m) & 31) && n < a.N) {
+                const int64_t o = static_cast<int64_t>(m) * a.N + n;
+                if (a.acc) a.acc[o] = v;
+                if constexpr (FUSED) {
+                    const float d = __fmul_rn(__fmul_rn(__int2float_rn(v), wsc[j]), xscale_s[m]);
+                    a.out[o] = __float2half_rn(d);
+                }
+            }
+        }
+}
+
+// ---- int8 GEMV over the reference's [K][N] weights --------------------------------
+// Thread = 16 consecutive columns (one 16-byte load per k row); four rows are
+// loaded together and transposed with byte permutes so DP4A can consume
+// column words.  4 threads span 64 columns, 64 threads split K.
+constexpr int kKnTx = 4;
+constexpr int kKnTy = 64;
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+template <int M>
+__global__ void __launch_bounds__(kKnTx * kKnTy)
+w8_kn_kernel(const int8_t* __restrict__ xq, const int8_t* __restrict__ w, int32_t* __restrict__ acc_out,
+             int K, int N) {
+    extern __shared__ int red_i[];  // [kKnTy/8 warps][M][64]
+    const int tx = threadIdx.x % kKnTx;
+    const int ty = threadIdx.x / kKnTx;
+    const int nb = blockIdx.x * (kKnTx * 16);
+    const int n0 = nb + tx * 16;
+    pdl_trigger();
+    pdl_wait();
+    int acc[M][16];
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+#pragma unroll
+        for (int e = 0; e < 16; ++e) acc[m][e] = 0;
+    if (n0 < N) {
+        for (int k = ty * 4; k < K; k += kKnTy * 4) {
+            uint4 r[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) r[t] = ld_stream(w + static_cast<int64_t>(k + t) * N + n0);
+            uint32_t xw[M];
+#pragma unroll
+            for (int m = 0; m < M; ++m) xw[m] = *reinterpret_cast<const uint32_t*>(xq + static_cast<int64_t>(m) * K + k);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t a0 = q == 0 ? r[0].x : q == 1 ? r[0].y : q == 2 ? r[0].z : r[0].w;
+                const uint32_t a1 = q == 0 ? r[1].x : q == 1 ? r[1].y : q == 2 ? r[1].z : r[1].w;
+                const uint32_t a2 = q == 0 ? r[2].x : q == 1 ? r[2].y : q == 2 ? r[2].z : r[2].w;
+                const uint32_t a3 = q == 0 ? r[3].x : q == 1 ? r[3].y : q == 2 ? r[3].z : r[3].w;
+                // 4x4 byte transpose: column c of this word group = bytes c of a0..a3
+                const uint32_t t0 = prmt(a0, a1, 0x5140);
+                const uint32_t t1 = prmt(a2, a3, 0x5140);
+                const uint32_t t2 = prmt(a0, a1, 0x7362);
+                const uint32_t t3 = prmt(a2, a3, 0x7362);
+                const uint32_t c0 = prmt(t0, t1, 0x5410);
+                const uint32_t c1 = prmt(t0, t1, 0x7632);
+                const uint32_t c2 = prmt(t2, t3, 0x5410);
+                const uint32_t c3 = prmt(t2, t3, 0x7632);
+#pragma unroll
+                for (int m = 0; m < M; ++m) {
+                    acc[m][4 * q + 0] = __dp4a(static_cast<int>(c0), static_cast<int>(xw[m]), acc[m][4 * q + 0]);
+                    acc[m][4 * q + 1] = __dp4a(static_cast<int>(c1), static_cast<int>(xw[m]), acc[m][4 * q + 1]);
+                    acc[m][4 * q + 2] = __dp4a(static_cast<int>(c2), static_cast<int>(xw[m]), acc[m][4 * q + 2]);
+                    acc[m][4 * q + 3] = __dp4a(static_cast<int>(c3), static_cast<int>(xw[m]), acc[m][4 * q + 3]);
+                }
+            }
+        }
+    }
+    // reduce over the 8 ty values inside each warp (lanes differing in bits 2..4)
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            int v = acc[m][e];
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 16);
+            acc[m][e] = v;
+        }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane < kKnTx) {
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+#pragma unroll
+            for (int e = 0; e < 16; ++e) red_i[(warp * M + m) * 64 + lane * 16 + e] = acc[m][e];
+    }
+    __syncthreads();
+    for (int o = threadIdx.x; o < M * 64; o += kKnTx * kKnTy) {
+        const int m = o / 64, col = o % 64;
+        int s = 0;
+        for (int wi = 0; wi < (kKnTx * kKnTy) / 32; ++wi) s += red_i[(wi * M + m) * 64 + col];
+        const int n = nb + col;
+        if (n < N) acc_out[static_cast<int64_t>(m) * N + n] = s;
+    }
+}
+
+__global__ void dequant_kernel(const int32_t* __restrict__ acc, const __half* __restrict__ xs,
+                               const __half* __restrict__ ws, __half* __restrict__ out, int M, int N) {
+    pdl_trigger();
+    pdl_wait();
+    const int64_t total = static_cast<int64_t>(M) * N;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int m = static_cast<int>(i / N), n = static_cast<int>(i % N);
+        const float d = __fmul_rn(__fmul_rn(__int2float_rn(acc[i]), __half2float(ws[n])), __half2float(xs[m]));
+        out[i] = __float2half_rn(d);
+    }
+}
+
+// fp32 -> fp16 by truncation, underflow to signed zero: the reference's
+// host-side scale conversion (src/csrc/lib/quantized_weight.cpp:186-195).
+__device__ __forceinline__ uint16_t f32_to_f16_trunc(float f) {
+    const uint32_t x = __float_as_uint(f);
+    const uint16_t sign = static_cast<uint16_t>((x >> 16) & 0x8000u);
+    const int e = static_cast<int>((x >> 23) & 0xffu) - 112;
+    if (e <= 0) return sign;
+    if (e >= 31) return static_cast<uint16_t>(sign | 0x7c00u);
+    return static_cast<uint16_t>(sign | (e << 10) | ((x & 0x7fffffu) >> 13));
+}
+
+// One thread per output column n; reads the [K][N] fp16 source coalesced.
+__global__ void quantize_weight_kernel(const __half* __restrict__ w, int8_t* __restrict__ wq,
+                                       __half* __restrict__ w_scale, int K, int N, int layout) {
+    pdl_trigger();
+    pdl_wait();
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    float mx = 0.0f;
+    for (int k = 0; k < K; ++k) mx = fmaxf(mx, fabsf(__half2float(w[static_cast<int64_t>(k) * N + n])));
+    const float scale = scale_from_absmax(mx);
+    const float inv = __fdiv_rn(1.0f, scale);
+    w_scale[n] = __ushort_as_half(f32_to_f16_trunc(scale));
+    for (int k = 0; k < K; ++k) {
+        float q = __fmul_rn(__half2float(w[static_cast<int64_t>(k) * N + n]), inv);
+        q = q > 127.0f ? 127.0f : q;
+        q = q < -128.0f ? -128.0f : q;
+        q = q >= 0.0f ? __fadd_rn(q, 0.5f) : __fsub_rn(q, 0.5f);
+        const int8_t v = static_cast<int8_t>(__float2int_rz(q));
+        if (layout == 0) wq[static_cast<int64_t>(n) * K + k] = v;
+        else wq[static_cast<int64_t>(k) * N + n] = v;
+    }
+}
+
+template <int M, bool FUSED>
+int launch_w8_rows_m(const W8Args& a, cudaStream_t s) {
+    const int chunks_per_lane = (a.K / 16 + 31) / 32;
+    int kch = 1;
+    while (kch < chunks_per_lane) kch *= 2;
+    const dim3 grid((a.N + kW8Warps * kW8Cpw - 1) / (kW8Warps * kW8Cpw));
+    const dim3 block(kW8Warps * 32);
+    const size_t smem = static_cast<size_t>(M) * a.K;
+    auto go = [&](auto kern) -> int {
+        if (smem > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w8_rows)");
+        }
+        return launch(kern, grid, block, smem, s, a);
+    };
+    switch (kch) {
+        case 1: return go(w8_rows_kernel<M, 1, FUSED>);
+        case 2: return go(w8_rows_kernel<M, 2, FUSED>);
+        case 4: return go(w8_rows_kernel<M, 4, FUSED>);
+        case 8: return go(w8_rows_kernel<M, 8, FUSED>);
+        default: return fail(MCV_ERR_SHAPE, "w8a8: K above 16384 unsupported");
+    }
+}
+
+template <bool FUSED>
+int launch_w8_rows(int64_t M, const W8Args& a, cudaStream_t s) {
+    switch (M) {
+        case 1: return launch_w8_rows_m<1, FUSED>(a, s);
+        case 2: return launch_w8_rows_m<2, FUSED>(a, s);
+        case 3: return launch_w8_rows_m<3, FUSED>(a, s);
+        case 4: return launch_w8_rows_m<4, FUSED>(a, s);
+        case 5: return launch_w8_rows_m<5, FUSED>(a, s);
+        case 6: return launch_w8_rows_m<6, FUSED>(a, s);
+        case 7: return launch_w8_rows_m<7, FUSED>(a, s);
+        default: return launch_w8_rows_m<8, FUSED>(a, s);
+    }
+}
+
+int launch_w8_kn(int64_t M, const int8_t* xq, const int8_t* w, int32_t* acc, int K, int N, cudaStream_t s) {
+    const dim3 grid((N + kKnTx * 16 - 1) / (kKnTx * 16));
+    const dim3 block(kKnTx * kKnTy);
+    const size_t smem = static_cast<size_t>((kKnTx * kKnTy) / 32) * M * 64 * sizeof(int);
+    switch (M) {
+        case 1: return launch(w8_kn_kernel<1>, grid, block, smem, s, xq, w, acc, K, N);
+        case 2: return launch(w8_kn_kernel<2>, grid, block, smem, s, xq, w, acc, K, N);
+        case 3: return launch(w8_kn_kernel<3>, grid, block, smem, s, xq, w, acc, K, N);
+        case 4: return launch(w8_kn_kernel<4>, grid, block, smem, s, xq, w, acc, K, N);
+        case 5: return launch(w8_kn_kernel<5>, grid, block, smem, s, xq, w, acc, K, N);
+        case 6: return launch(w8_kn_kernel<6>, grid, block, smem, s, xq, w, acc, K, N);
+        case 7: return launch(w8_kn_kernel<7>, grid, block, smem, s, xq, w, acc, K, N);
+        default: return launch(w8_kn_kernel<8>, grid, block, smem, s, xq, w, acc, K, N);
+    }
+}
+
+int check_mkn(int64_t M, int64_t K, int64_t N) {
+    if (M < 1 || M > 8) return fail(MCV_ERR_SHAPE, "w8a8: M must be 1..8");
+    if (K <= 0 || N <= 0 || K % 16 != 0) return fail(MCV_ERR_SHAPE, "w8a8: K must be a positive multiple of 16, N positive");
+    if (K > 16384 || N > (1 << 30)) return fail(MCV_ERR_SHAPE, "w8a8: dimension too large");
+    return MCV_OK;
+}
+
+int launch_dequant(const void* acc, const void* xs, const void* ws, void* out, int64_t M, int64_t N, cudaStream_t s) {
+    const int64_t total = M * N;
+    int64_t blocks = (total + 255) / 256;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+    if (blocks > cap) blocks = cap;
+    return launch(dequant_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s,
+                  static_cast<const int32_t*>(acc), static_cast<const __half*>(xs),
+                  static_cast<const __half*>(ws), static_cast<__half*>(out), static_cast<int>(M),
+                  static_cast<int>(N));
+}
+
+}  // namespace
+}  // namespace mcv
+
+using namespace mcv;
+
+extern "C" {
+
+int mcv_w8a8_quantize(const void* x, void* x_int8, void* x_scale, int64_t M, int64_t K, mcv_stream_t stream) {
+    if (!x || !x_int8 || !x_scale) return fail(MCV_ERR_NULL, "w8a8_quantize: null pointer");
+    if (M < 1 || M > 65535 || K < 1 || K > (1 << 30)) return fail(MCV_ERR_SHAPE, "w8a8_quantize: bad shape");
+    return launch(quantize_rows_kernel, dim3(static_cast<unsigned>(M)), dim3(kQThreads), 0,
+                  static_cast<cudaStream_t>(stream), static_cast<const __half*>(x), static_cast<int8_t*>(x_int8),
+                  static_cast<__half*>(x_scale), static_cast<int>(K));
+}
+
+int mcv_w8a8_gemm_i32(const void* x_int8, const void* w_int8, void* acc, int64_t M, int64_t K, int64_t N,
+                      int w_layout, mcv_stream_t stream) {
+    if (!x_int8 || !w_int8 || !acc) return fail(MCV_ERR_NULL, "w8a8_gemm_i32: null pointer");
+    int st = check_mkn(M, K, N);
+    if (st) return st;
+    auto s = static_cast<cudaStream_t>(stream);
+    if (w_layout == 0) {
+        if (!aligned16(x_int8) || !aligned16(w_int8)) return fail(MCV_ERR_ALIGN, "w8a8_gemm_i32: x and w must be 16-byte aligned");
+        W8Args a{};
+        a.x = x_int8;
+        a.w = static_cast<const int8_t*>(w_int8);
+        a.acc = static_cast<int32_t*>(acc);
+        a.K = static_cast<int>(K);
+        a.N = static_cast<int>(N);
+        return launch_w8_rows<false>(M, a, s);
+    }
+    if (w_layout != 1) return fail(MCV_ERR_VALUE, "w8a8_gemm_i32: w_layout must be 0 ([N][K]) or 1 ([K][N])");
+    if (N % 16 != 0) return fail(MCV_ERR_SHAPE, "w8a8_gemm_i32: [K][N] layout needs N % 16 == 0");
+    if (!aligned16(w_int8) || (reinterpret_cast<uintptr_t>(x_int8) & 3u))
+        return fail(MCV_ERR_ALIGN, "w8a8_gemm_i32: w must be 16-byte and x 4-byte aligned");
+    return launch_w8_kn(M, static_cast<const int8_t*>(x_int8), static_cast<const int8_t*>(w_int8),
+                        static_cast<int32_t*>(acc), static_cast<int>(K), static_cast<int>(N), s);
+}
+
+int mcv_w8a8_dequant(const void* acc, const void* x_scale, const void* w_scale, void* out, int64_t M, int64_t N,
+                     mcv_stream_t stream) {
+    if (!acc || !x_scale || !w_scale || !out) return fail(MCV_ERR_NULL, "w8a8_dequant: null pointer");
+    if (M < 1 || N < 1 || M * N > (int64_t(1) << 40) || N > (1 << 30) || M > (1 << 30))
+        return fail(MCV_ERR_SHAPE, "w8a8_dequant: bad shape");
+    return launch_dequant(acc, x_scale, w_scale, out, M, N, static_cast<cudaStream_t>(stream));
+}
+
+int mcv_w8a8_fused(const void* x, const void* w_int8, const void* w_scale, void* out, void* acc_out,
+                   void* x_int8_out, void* x_scale_out, int64_t M, int64_t K, int64_t N, int w_layout,
+                   mcv_stream_t stream) {
+    if (!x || !w_int8 || !w_scale || !out) return fail(MCV_ERR_NULL, "w8a8_fused: null pointer");
+    int st = check_mkn(M, K, N);
+    if (st) return st;
+    auto s = static_cast<cudaStream_t>(stream);
+    if (w_layout == 0) {
+        if (!aligned16(w_int8)) return fail(MCV_ERR_ALIGN, "w8a8_fused: w must be 16-byte aligned");
+        W8Args a{};
+        a.x = x;
+        a.w = static_cast<const int8_t*>(w_int8);
+        a.w_scale = static_cast<const __half*>(w_scale);
+        a.out = static_cast<__half*>(out);
+        a.acc = static_cast<int32_t*>(acc_out);
+        a.xq_out = static_cast<int8_t*>(x_int8_out);
+        a.xs_out = static_cast<__half*>(x_scale_out);
+        a.K = static_cast<int>(K);
+        a.N = static_cast<int>(N);
+        return launch_w8_rows<true>(M, a, s);
+    }
+    if (w_layout != 1) return fail(MCV_ERR_VALUE, "w8a8_fused: w_layout must be 0 or 1");
+    if (!acc_out || !x_int8_out || !x_scale_out)
+        return fail(MCV_ERR_WORKSPACE, "w8a8_fused: the [K][N] path needs acc_out, x_int8_out and x_scale_out buffers");
+    st = mcv_w8a8_quantize(x, x_int8_out, x_scale_out, M, K, stream);
+    if (st) return st;
+    st = mcv_w8a8_gemm_i32(x_int8_out, w_int8, acc_out, M, K, N, 1, stream);
+    if (st) return st;
+    return launch_dequant(acc_out, x_scale_out, w_scale, out, M, N, s);
+}
+
+int mcv_w8a8_quantize_weight(const void* w_kn, void* wq, void* w_scale, int64_t K, int64_t N, int w_layout,
+                             mcv_stream_t stream) {
+    if (!w_kn || !wq || !w_scale) return fail(MCV_ERR_NULL, "w8a8_quantize_weight: null pointer");
+    if (K < 1 || N < 1 || K > (1 << 30) || N > (1 << 30)) return fail(MCV_ERR_SHAPE, "w8a8_quantize_weight: bad shape");
+    if (w_layout != 0 && w_layout != 1) return fail(MCV_ERR_VALUE, "w8a8_quantize_weight: w_layout must be 0 or 1");
+    return launch(quantize_weight_kernel, dim3(static_cast<unsigned>((N + 127) / 128)), dim3(128), 0,
+                  static_cast<cudaStream_t>(stream), static_cast<const __half*>(w_kn), static_cast<int8_t*>(wq),
+                  static_cast<__half*>(w_scale), static_cast<int>(K), static_cast<int>(N), w_layout);
+}
+
+}  // extern "C"

@@ -1,0 +1,321 @@
+"""Python binding of libmcv_b200.so (the C ABI in include/mcv_matmul.h).
+
+The functions mirror the reference engine's op surface for the decode matmul
+path (src/csrc/include/minicpmv/ops.h of lvyufeng/minicpm-v-4.6-orangepi):
+``matmul_w4a16``, ``matmul_b_transposed``, ``argmax_last_dim``,
+``matmul_w8a8_i32``, ``w8a8_quantize``, ``w8a8_dequant``, plus the fused
+``lm_head_argmax`` that replaces lm_head_greedy's chunk loop, and the
+load-time weight preparation of quantized_weight.h.  As in the reference,
+outputs are caller-allocated tensors and a failed check raises RuntimeError.
+
+torch is only the device-memory and stream plumbing here: every computation
+is one of the library's CUDA kernels, reached through ctypes with raw device
+pointers.  There is no CPU fallback; importing without the built library or
+calling without a CUDA device fails loudly.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+_PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(_PKG_DIR, "libmcv_b200.so")
+_lib = None
+
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_vp = ctypes.c_void_p
+_sz = ctypes.c_size_t
+
+# name -> argtypes (restype int unless listed in _RESTYPE)
+_SIGS = {
+    "mcv_status_string": [_int],
+    "mcv_last_error": [],
+    "mcv_version": [],
+    "mcv_set_pdl": [_int],
+    "mcv_w4a16_layout_bytes": [_i64, _i64, _i64, _vp, _vp, _vp],
+    "mcv_w4a16_pack_host": [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp],
+    "mcv_w4a16_pack_gptq_host": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp],
+    "mcv_w4a16_pack_awq_host": [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp],
+    "mcv_w4a16_pack_from_tiles_host": [_vp, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _vp],
+    "mcv_w4a16_gemv": [_vp, _vp, _vp, _vp, _int, _vp, _i64, _i64, _i64, _i64, _vp],
+    "mcv_gemv_f16": [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
+    "mcv_lm_head_workspace_size": [_i64],
+    "mcv_lm_head_argmax": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _sz, _vp],
+    "mcv_argmax_last_dim_f16": [_vp, _vp, _i64, _i64, _vp],
+    "mcv_argmax_key_to_index": [_vp, _vp, _i64, _vp],
+    "mcv_nccl_unique_id_bytes": [],
+    "mcv_nccl_get_unique_id": [_vp],
+    "mcv_nccl_comm_init": [_vp, _int, _vp, _int],
+    "mcv_nccl_comm_destroy": [_vp],
+    "mcv_lm_head_argmax_allreduce": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _sz, _vp],
+    "mcv_w8a8_quantize": [_vp, _vp, _vp, _i64, _i64, _vp],
+    "mcv_w8a8_gemm_i32": [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
+    "mcv_w8a8_dequant": [_vp, _vp, _vp, _vp, _i64, _i64, _vp],
+    "mcv_w8a8_fused": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
+    "mcv_w8a8_quantize_weight": [_vp, _vp, _vp, _i64, _i64, _int, _vp],
+}
+_RESTYPE = {
+    "mcv_status_string": ctypes.c_char_p,
+    "mcv_last_error": ctypes.c_char_p,
+    "mcv_set_pdl": None,
+    "mcv_lm_head_workspace_size": _sz,
+    "mcv_nccl_unique_id_bytes": _sz,
+}
+EXPORTED = tuple(_SIGS)
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"libmcv_b200.so not built ({LIB_PATH}); run __graft_entry__.build()")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, args in _SIGS.items():
+            f = getattr(L, name)
+            f.argtypes = args
+            f.restype = _RESTYPE.get(name, _int)
+        _lib = L
+    return _lib
+
+
+class McvError(RuntimeError):
+    def __init__(self, status: int, where: str):
+        L = lib()
+        msg = L.mcv_last_error().decode(errors="replace")
+        super().__init__(f"{where}: {L.mcv_status_string(status).decode()} ({status}): {msg}")
+        self.status = status
+
+
+def _check(status: int, where: str) -> None:
+    if status != 0:
+        raise McvError(status, where)
+
+
+def _stream(stream=None):
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return _vp(stream.cuda_stream)
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    if isinstance(t, np.ndarray):
+        return t.ctypes.data_as(_vp)
+    if not t.is_cuda:
+        raise RuntimeError("mcv_b200: expected a CUDA tensor")
+    if not t.is_contiguous():
+        raise RuntimeError("mcv_b200: tensors must be contiguous")
+    return _vp(t.data_ptr())
+
+
+def set_pdl(enabled: bool) -> None:
+    lib().mcv_set_pdl(1 if enabled else 0)
+
+
+# ---- W4A16 ------------------------------------------------------------------
+
+@dataclass
+class W4A16QuantizedWeight:
+    """Device weight in the mcv-int4 layout (counterpart of the reference's
+    W4A16QuantizedWeight, src/csrc/include/minicpmv/quantized_weight.h:11-17)."""
+    qweight: object   # torch.int32 [N, K/8]
+    scales: object    # torch.float16 [N, K/group]
+    zeros: object     # torch.int32 [N, ceil(G/8)]
+    zero_bias: int
+    K: int
+    N: int
+    group_size: int = 128
+
+    @property
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.qweight, self.scales, self.zeros))
+
+
+def _alloc_layout_host(K: int, N: int, group: int):
+    G = K // group
+    qw = np.empty((N, K // 8), np.uint32)
+    sc = np.empty((N, G), np.uint16)
+    zw = np.empty((N, (G + 7) // 8), np.uint32)
+    return qw, sc, zw
+
+
+def _to_device(qw, sc, zw, zero_bias, K, N, group, device) -> W4A16QuantizedWeight:
+    import torch
+    return W4A16QuantizedWeight(
+        torch.from_numpy(qw.view(np.int32)).to(device),
+        torch.from_numpy(sc.view(np.float16)).to(device),
+        torch.from_numpy(zw.view(np.int32)).to(device),
+        int(zero_bias), K, N, group)
+
+
+def pack_w4a16(q_kn: np.ndarray, z_gn: np.ndarray, scales_gn: np.ndarray, group: int = 128,
+               device="cuda") -> W4A16QuantizedWeight:
+    """Logical q uint8 [K,N] (0..15), z uint8 [G,N], scales fp16 [G,N] -> device layout."""
+    q = np.ascontiguousarray(q_kn, np.uint8)
+    z = np.ascontiguousarray(z_gn, np.uint8)
+    s = np.ascontiguousarray(scales_gn).view(np.uint16)
+    K, N = q.shape
+    qw, sc, zw = _alloc_layout_host(K, N, group)
+    _check(lib().mcv_w4a16_pack_host(_ptr(q), _ptr(z), _ptr(s), K, N, group, _ptr(qw), _ptr(sc), _ptr(zw)),
+           "pack_w4a16")
+    return _to_device(qw, sc, zw, 0, K, N, group, device)
+
+
+def pack_w4a16_gptq(qweight, qzeros, g_idx, scales, group: int = 128, device="cuda") -> W4A16QuantizedWeight:
+    """GPTQ tensors (qweight int32 [K/8,N], qzeros int32 [G,N/8], g_idx int32 [K] or None,
+    scales fp16 [G,N]) -> device layout; load_w4a16_quantized_weight's GPTQ branch."""
+    qwt = np.ascontiguousarray(qweight, np.int32)
+    qz = np.ascontiguousarray(qzeros, np.int32)
+    gi = None if g_idx is None else np.ascontiguousarray(g_idx, np.int32)
+    s = np.ascontiguousarray(scales).view(np.uint16)
+    K, N = qwt.shape[0] * 8, qwt.shape[1]
+    qw, sc, zw = _alloc_layout_host(K, N, group)
+    zb = ctypes.c_int(0)
+    _check(lib().mcv_w4a16_pack_gptq_host(_ptr(qwt), _ptr(qz), _ptr(gi) if gi is not None else None, _ptr(s),
+                                          K, N, group, _ptr(qw), _ptr(sc), _ptr(zw), ctypes.byref(zb)),
+           "pack_w4a16_gptq")
+    return _to_device(qw, sc, zw, zb.value, K, N, group, device)
+
+
+def pack_w4a16_awq(qweight, qzeros, scales, group: int = 128, device="cuda") -> W4A16QuantizedWeight:
+    """AWQ tensors (qweight int32 [K,N/8], qzeros int32 [G,N/8], scales fp16 [G,N])."""
+    qwt = np.ascontiguousarray(qweight, np.int32)
+    qz = np.ascontiguousarray(qzeros, np.int32)
+    s = np.ascontiguousarray(scales).view(np.uint16)
+    K, N = qwt.shape[0], qwt.shape[1] * 8
+    qw, sc, zw = _alloc_layout_host(K, N, group)
+    zb = ctypes.c_int(0)
+    _check(lib().mcv_w4a16_pack_awq_host(_ptr(qwt), _ptr(qz), _ptr(s), K, N, group, _ptr(qw), _ptr(sc),
+                                         _ptr(zw), ctypes.byref(zb)), "pack_w4a16_awq")
+    return _to_device(qw, sc, zw, zb.value, K, N, group, device)
+
+
+def pack_w4a16_from_tiles(packed: np.ndarray, scales_gn: np.ndarray, K: int, N: int,
+                          device="cuda") -> W4A16QuantizedWeight:
+    """The reference's tile-packed int8 (q - zero) [rows, tile_len] + scales [G,N]."""
+    p = np.ascontiguousarray(packed, np.int8)
+    s = np.ascontiguousarray(scales_gn).view(np.uint16)
+    qw, sc, zw = _alloc_layout_host(K, N, 128)
+    zb = ctypes.c_int(0)
+    _check(lib().mcv_w4a16_pack_from_tiles_host(_ptr(p), p.shape[1], _ptr(s), K, N, _ptr(qw), _ptr(sc),
+                                                _ptr(zw), ctypes.byref(zb)), "pack_w4a16_from_tiles")
+    return _to_device(qw, sc, zw, zb.value, K, N, 128, device)
+
+
+def matmul_w4a16(x, w: W4A16QuantizedWeight, out, stream=None) -> None:
+    """out fp16 [M,N] = x fp16 [M,K] @ dequant(w); M = 1..8 (ops.h:95-108)."""
+    M = x.shape[0] if x.dim() == 2 else 1
+    _check(lib().mcv_w4a16_gemv(_ptr(x), _ptr(w.qweight), _ptr(w.scales), _ptr(w.zeros), w.zero_bias, _ptr(out),
+                                M, w.K, w.N, w.group_size, _stream(stream)), "matmul_w4a16")
+
+
+# ---- dense fp16 ----------------------------------------------------------------
+
+def matmul_b_transposed(a, b, out, stream=None) -> None:
+    """out [M,N] = a [M,K] @ B with b stored [N,K] or [K,N], as the reference
+    disambiguates them (src/csrc/lib/ops.cpp:165-171); M = 1..8."""
+    M, K = a.shape
+    if b.shape[1] == K:
+        layout, N = 0, b.shape[0]
+    elif b.shape[0] == K:
+        layout, N = 1, b.shape[1]
+    else:
+        raise RuntimeError("matmul_b_transposed K dim mismatch")
+    if tuple(out.shape) != (M, N):
+        raise RuntimeError("matmul_b_transposed out shape mismatch")
+    _check(lib().mcv_gemv_f16(_ptr(a), _ptr(b), _ptr(out), M, K, N, layout, _stream(stream)), "matmul_b_transposed")
+
+
+def lm_head_workspace(M: int = 1, device="cuda"):
+    import torch
+    n = int(lib().mcv_lm_head_workspace_size(M))
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+def lm_head_argmax(x, w_nk, workspace, out_index=None, out_key=None, n_offset: int = 0,
+                   fp16_logits: bool = False, stream=None) -> None:
+    """Fused lm_head GEMV + greedy argmax over rows of w_nk fp16 [N_shard,K]."""
+    M, K = x.shape
+    N = w_nk.shape[0]
+    _check(lib().mcv_lm_head_argmax(_ptr(x), _ptr(w_nk), _ptr(out_key), _ptr(out_index), M, K, N, n_offset,
+                                    int(fp16_logits), _ptr(workspace), workspace.numel(), _stream(stream)),
+           "lm_head_argmax")
+
+
+def argmax_last_dim(logits, out, stream=None) -> None:
+    """int64 [M] = argmax over the last dim of fp16 [M,V] (ops.h:21)."""
+    M, V = logits.shape
+    _check(lib().mcv_argmax_last_dim_f16(_ptr(logits), _ptr(out), M, V, _stream(stream)), "argmax_last_dim")
+
+
+# ---- sharded lm_head ------------------------------------------------------------
+
+class NcclComm:
+    """An NCCL communicator owned by the library (one rank per process/GPU)."""
+
+    def __init__(self, nranks: int, rank: int, unique_id: bytes):
+        self.handle = _vp()
+        _check(lib().mcv_nccl_comm_init(ctypes.byref(self.handle), nranks, unique_id, rank), "nccl_comm_init")
+
+    @staticmethod
+    def unique_id() -> bytes:
+        n = int(lib().mcv_nccl_unique_id_bytes())
+        buf = ctypes.create_string_buffer(n)
+        _check(lib().mcv_nccl_get_unique_id(buf), "nccl_get_unique_id")
+        return buf.raw
+
+    def destroy(self) -> None:
+        if self.handle:
+            _check(lib().mcv_nccl_comm_destroy(self.handle), "nccl_comm_destroy")
+            self.handle = _vp()
+
+
+def lm_head_argmax_allreduce(comm: NcclComm, x, w_shard, workspace, out_key, out_index, n_offset: int,
+                             fp16_logits: bool = False, stream=None) -> None:
+    M, K = x.shape
+    _check(lib().mcv_lm_head_argmax_allreduce(comm.handle, _ptr(x), _ptr(w_shard), _ptr(out_key), _ptr(out_index),
+                                              M, K, w_shard.shape[0], n_offset, int(fp16_logits),
+                                              _ptr(workspace), workspace.numel(), _stream(stream)),
+           "lm_head_argmax_allreduce")
+
+
+# ---- W8A8 -----------------------------------------------------------------------
+
+def w8a8_quantize(x, x_int8, x_scale, stream=None) -> None:
+    M, K = x.shape
+    _check(lib().mcv_w8a8_quantize(_ptr(x), _ptr(x_int8), _ptr(x_scale), M, K, _stream(stream)), "w8a8_quantize")
+
+
+def matmul_w8a8_i32(x_int8, w_int8, out, w_layout: int = 1, stream=None) -> None:
+    """int32 [M,N] = int8 [M,K] @ int8 weights; layout 1 = [K,N] (reference), 0 = [N,K]."""
+    M, K = x_int8.shape
+    N = w_int8.shape[1] if w_layout == 1 else w_int8.shape[0]
+    _check(lib().mcv_w8a8_gemm_i32(_ptr(x_int8), _ptr(w_int8), _ptr(out), M, K, N, w_layout, _stream(stream)),
+           "matmul_w8a8_i32")
+
+
+def w8a8_dequant(acc, x_scale, w_scale, out, stream=None) -> None:
+    M, N = acc.shape
+    _check(lib().mcv_w8a8_dequant(_ptr(acc), _ptr(x_scale), _ptr(w_scale), _ptr(out), M, N, _stream(stream)),
+           "w8a8_dequant")
+
+
+def w8a8_fused(x, w_int8, w_scale, out, acc=None, x_int8=None, x_scale=None, w_layout: int = 0,
+               stream=None) -> None:
+    M, K = x.shape
+    N = w_int8.shape[0] if w_layout == 0 else w_int8.shape[1]
+    _check(lib().mcv_w8a8_fused(_ptr(x), _ptr(w_int8), _ptr(w_scale), _ptr(out), _ptr(acc), _ptr(x_int8),
+                                _ptr(x_scale), M, K, N, w_layout, _stream(stream)), "w8a8_fused")
+
+
+def quantize_dense_weight_w8a8(w_kn, wq, w_scale, w_layout: int = 0, stream=None) -> None:
+    K, N = w_kn.shape
+    _check(lib().mcv_w8a8_quantize_weight(_ptr(w_kn), _ptr(wq), _ptr(w_scale), K, N, w_layout, _stream(stream)),
+           "quantize_dense_weight_w8a8")

@@ -1,0 +1,163 @@
+"""Dense fp16 GEMV, fused lm_head argmax and argmax_last_dim on the GPU vs the
+CPU oracle / reference golden outputs.  fp16 outputs: |d| <= 1e-2 + 1e-3|ref|;
+argmax indices: exact."""
+import numpy as np
+import pytest
+
+import make_golden as golden
+import oracle
+from conftest import assert_f16_close
+from mcv_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(torch, a, dtype=None):
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint16:
+        a = a.view(np.float16)
+    return torch.from_numpy(a).cuda()
+
+
+def gemv(torch, x, w, layout):
+    import mcv_b200
+    xd, wd = dev(torch, x), dev(torch, w)
+    N = w.shape[0] if layout == 0 else w.shape[1]
+    out = torch.empty((xd.shape[0], N), dtype=torch.float16, device="cuda")
+    mcv_b200.matmul_b_transposed(xd, wd, out)
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def lm_head(torch, x, w_nk, n_offset=0, fp16_logits=False):
+    import mcv_b200
+    xd, wd = dev(torch, x), dev(torch, w_nk)
+    M = xd.shape[0]
+    ws = mcv_b200.lm_head_workspace(M)
+    idx = torch.empty(M, dtype=torch.int64, device="cuda")
+    key = torch.empty(M, dtype=torch.int64, device="cuda")
+    mcv_b200.lm_head_argmax(xd, wd, ws, out_index=idx, out_key=key, n_offset=n_offset, fp16_logits=fp16_logits)
+    torch.cuda.synchronize()
+    return idx.cpu().numpy(), key.cpu().numpy().view(np.uint64), ws
+
+
+def test_cube_golden(cuda):
+    out = gemv(cuda, golden.load("cube.x"), golden.load("cube.w_nk"), 0)
+    assert_f16_close(out, golden.load("cube.ref"), what="cube")
+
+
+@pytest.mark.parametrize("tag", ["matmul_4x128x64", "matmul_1x1024x4096"])
+def test_matmul_golden_natural_layout(cuda, tag):
+    # [K,N] "natural" B; K=128,N=64 collides with neither disambiguation rule
+    out = gemv(cuda, golden.load(tag + ".x"), golden.load(tag + ".w_kn"), 1)
+    assert_f16_close(out, golden.load(tag + ".ref"), what=tag)
+
+
+@pytest.mark.parametrize("M", [1, 3, 8])
+@pytest.mark.parametrize("layout", [0, 1])
+def test_gemv_vs_oracle(cuda, M, layout):
+    r = synth.rng(M * 10 + layout)
+    K, N = 1024, 3584
+    x = r.standard_normal((M, K), dtype=np.float32).astype(np.float16)
+    w = (r.standard_normal((N, K) if layout == 0 else (K, N), dtype=np.float32) * 0.05).astype(np.float16)
+    ref = oracle.gemv_f16(x, w, layout=layout)
+    assert_f16_close(gemv(cuda, x, w, layout), ref, what=f"gemv M={M} layout={layout}")
+
+
+def test_lm_head_pipeline_golden(cuda):
+    # tests/test_lm_head_pipeline.cpp: 4 rows, H=64, V=128, weight [H,V]
+    w_nk = np.ascontiguousarray(golden.load("lm_head.w").T)
+    idx, _, _ = lm_head(cuda, golden.load("lm_head.x"), w_nk)
+    assert np.array_equal(idx, golden.load("lm_head.ref"))
+
+
+@pytest.fixture(scope="module")
+def vocab():
+    x, w = synth.lm_head_inputs(1024, 248094, seed=1)
+    return x, w
+
+
+def test_lm_head_full_vocab(cuda, vocab):
+    x, w = vocab
+    ref_idx, ref_best, gap = oracle.lm_head_argmax(x, w, nthreads=8)
+    assert gap[0] > 1e-4, "seed gives an ambiguous top-2; pick another"
+    idx, key, ws = lm_head(cuda, x, w)
+    assert idx[0] == ref_idx[0]
+    assert int(key[0]) == oracle.argmax_key(float(ref_best[0]), int(ref_idx[0])) or \
+        (int(key[0]) & 0xFFFFFFFF) == 0xFFFFFFFF - int(ref_idx[0])
+    # the workspace counter is left at zero for the next call
+    assert int(ws[:4].cpu().numpy().view(np.uint32)[0]) == 0
+    idx2, _, _ = lm_head(cuda, x, w)
+    assert idx2[0] == idx[0]
+
+
+def test_lm_head_fp16_logits_mode(cuda, vocab):
+    x, w = vocab
+    ref_idx, _, gap = oracle.lm_head_argmax(x, w, fp16_logits=True, nthreads=8)
+    idx, _, _ = lm_head(cuda, x, w, fp16_logits=True)
+    if gap[0] > 0:
+        assert idx[0] == ref_idx[0]
+
+
+@pytest.mark.parametrize("shards", [2, 4, 8])
+def test_lm_head_shards_combine(cuda, vocab, shards):
+    """Per-shard keys (contiguous ceil(V/g) row ranges with global offsets)
+    combine by max into the unsharded answer: the host side of the NCCL path."""
+    x, w = vocab
+    V = w.shape[0]
+    per = (V + shards - 1) // shards
+    keys = []
+    for r in range(shards):
+        a, b = r * per, min(V, (r + 1) * per)
+        _, k, _ = lm_head(cuda, x, np.ascontiguousarray(w[a:b]), n_offset=a)
+        keys.append(int(k[0]))
+    best = max(keys)
+    ref_idx, _, _ = oracle.lm_head_argmax(x, w, nthreads=8)
+    assert 0xFFFFFFFF - (best & 0xFFFFFFFF) == ref_idx[0]
+
+
+def test_lm_head_ties_first_max(cuda):
+    r = synth.rng(3)
+    K, N = 256, 5000
+    x = r.standard_normal((2, K), dtype=np.float32).astype(np.float16)
+    w = (r.standard_normal((N, K), dtype=np.float32) * 0.02).astype(np.float16)
+    w[4000] = w[1234] = np.float16(0.5) * np.sign(x[0]).astype(np.float16)  # identical best rows
+    idx, _, _ = lm_head(cuda, x, w)
+    ref, _, _ = oracle.lm_head_argmax(x, w)
+    assert idx[0] == 1234 and idx[0] == ref[0]
+    assert idx[1] == ref[1]
+    # all-zero weights: every logit is 0, the first row wins
+    idx0, _, _ = lm_head(cuda, x, np.zeros((777, K), np.float16))
+    assert list(idx0) == [0, 0]
+    # all logits negative
+    wn = -np.abs(w)
+    xp = np.abs(x)
+    idxn, _, _ = lm_head(cuda, xp, wn)
+    refn, _, _ = oracle.lm_head_argmax(xp, wn)
+    assert np.array_equal(idxn, refn)
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 1024, 1), (1, 8, 3), (3, 2048, 33333), (8, 1024, 4096)])
+def test_lm_head_shapes(cuda, M, K, N):
+    r = synth.rng(M + K + N)
+    x = r.standard_normal((M, K), dtype=np.float32).astype(np.float16)
+    w = (r.standard_normal((N, K), dtype=np.float32) * 0.02).astype(np.float16)
+    ref, _, gap = oracle.lm_head_argmax(x, w, nthreads=8)
+    idx, _, _ = lm_head(cuda, x, w)
+    for m in range(M):
+        if gap[m] > 1e-4 or N == 1:
+            assert idx[m] == ref[m], (m, idx[m], ref[m], gap[m])
+
+
+def test_argmax_last_dim(cuda):
+    import mcv_b200
+    torch = cuda
+    r = synth.rng(9)
+    logits = r.standard_normal((4, 50000), dtype=np.float32).astype(np.float16)
+    logits[2, 77] = logits[2, 900] = np.float16(60000)  # tie -> first
+    ld = torch.from_numpy(logits).cuda()
+    out = torch.empty(4, dtype=torch.int64, device="cuda")
+    mcv_b200.argmax_last_dim(ld, out)
+    torch.cuda.synchronize()
+    assert out.cpu().tolist() == np.argmax(logits.astype(np.float32), axis=1).tolist()
+    assert out[2].item() == 77

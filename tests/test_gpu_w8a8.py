@@ -1,0 +1,132 @@
+"""W8A8 on the GPU vs the CPU oracle: int8 quantized activations, int32
+accumulators and fp16 outputs must all be BIT-EXACT (the float steps use
+explicitly rounded fp32 operations in the same order as the reference)."""
+import numpy as np
+import pytest
+
+import make_golden as golden
+import oracle
+from mcv_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def D(torch, a):
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint16:
+        a = a.view(np.float16)
+    return torch.from_numpy(a).cuda()
+
+
+def H(t):
+    a = t.cpu().numpy()
+    return a.view(np.uint16) if a.dtype == np.float16 else a
+
+
+@pytest.mark.parametrize("layout", [1, 0])
+def test_i32_golden(cuda, layout):
+    import mcv_b200
+    torch = cuda
+    x = golden.load("w8a8_i32.x")
+    w = golden.load("w8a8_i32.w")
+    wl = w if layout == 1 else np.ascontiguousarray(w.T)
+    acc = torch.empty((1, 3584), dtype=torch.int32, device="cuda")
+    mcv_b200.matmul_w8a8_i32(D(torch, x), D(torch, wl), acc, w_layout=layout)
+    torch.cuda.synchronize()
+    assert np.array_equal(H(acc), golden.load("w8a8_i32.ref"))
+
+
+def test_dequant_golden(cuda):
+    import mcv_b200
+    torch = cuda
+    acc = golden.load("w8a8_dequant.acc")
+    xs = golden.load("w8a8_dequant.xs")
+    ws = golden.load("w8a8_dequant.ws")
+    out = torch.empty((1, 3584), dtype=torch.float16, device="cuda")
+    mcv_b200.w8a8_dequant(D(torch, acc), D(torch, xs), D(torch, ws), out)
+    torch.cuda.synchronize()
+    assert np.array_equal(H(out), oracle.w8a8_dequant(acc, xs, ws))
+    assert np.max(np.abs(H(out).view(np.float16).astype(np.float32) - golden.load("w8a8_dequant.ref"))) < 0.02
+
+
+@pytest.mark.parametrize("M", [1, 4, 8])
+def test_quantize_exact(cuda, M):
+    import mcv_b200
+    torch = cuda
+    x, _, _ = synth.w8a8_inputs(M, 1024, 16, seed=M)
+    x[0, :7] = np.float16([0.5, -0.5, 1e-4, -65504, 3.0, 0, -0.0])  # clamp / rounding edges
+    xq = torch.empty((M, 1024), dtype=torch.int8, device="cuda")
+    xs = torch.empty(M, dtype=torch.float16, device="cuda")
+    mcv_b200.w8a8_quantize(D(torch, x), xq, xs)
+    torch.cuda.synchronize()
+    rq, rs = oracle.w8a8_quantize(x)
+    assert np.array_equal(H(xq), rq)
+    assert np.array_equal(H(xs), rs)
+    z = torch.zeros((1, 256), dtype=torch.float16, device="cuda")
+    xq0 = torch.empty((1, 256), dtype=torch.int8, device="cuda")
+    xs0 = torch.empty(1, dtype=torch.float16, device="cuda")
+    mcv_b200.w8a8_quantize(z, xq0, xs0)
+    torch.cuda.synchronize()
+    assert np.all(H(xq0) == 0) and H(xs0)[0] == oracle.w8a8_quantize(np.zeros((1, 256), np.float16))[1][0]
+
+
+@pytest.mark.parametrize("M", [1, 4, 8])
+@pytest.mark.parametrize("N", [1024, 3584])
+@pytest.mark.parametrize("layout", [0, 1])
+def test_fused_config2_exact(cuda, M, N, layout):
+    import mcv_b200
+    torch = cuda
+    K = 1024
+    x, w, ws = synth.w8a8_inputs(M, K, N, seed=M * 100 + N)
+    racc, rout = oracle.w8a8_fused(x, w, ws, nthreads=8)
+    rq, rs = oracle.w8a8_quantize(x)
+    wl = np.ascontiguousarray(w.T) if layout == 0 else w
+    out = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    acc = torch.empty((M, N), dtype=torch.int32, device="cuda")
+    xq = torch.empty((M, K), dtype=torch.int8, device="cuda")
+    xs = torch.empty(M, dtype=torch.float16, device="cuda")
+    mcv_b200.w8a8_fused(D(torch, x), D(torch, wl), D(torch, ws), out, acc, xq, xs, w_layout=layout)
+    torch.cuda.synchronize()
+    assert np.array_equal(H(acc), racc)
+    assert np.array_equal(H(out), rout)
+    assert np.array_equal(H(xq), rq)
+    assert np.array_equal(H(xs), rs)
+    if layout == 0:  # optional intermediates may be omitted on the fast path
+        out2 = torch.empty((M, N), dtype=torch.float16, device="cuda")
+        mcv_b200.w8a8_fused(D(torch, x), D(torch, wl), D(torch, ws), out2, w_layout=0)
+        torch.cuda.synchronize()
+        assert np.array_equal(H(out2), rout)
+
+
+@pytest.mark.parametrize("K,N", [(1024, 3584), (2048, 1024), (4096, 16), (16, 48)])
+def test_gemm_shapes_exact(cuda, K, N):
+    import mcv_b200
+    torch = cuda
+    r = synth.rng(K + N)
+    M = 3
+    xq = r.integers(-128, 128, (M, K), dtype=np.int8)
+    w = r.integers(-128, 128, (K, N), dtype=np.int8)
+    ref = oracle.w8a8_gemm_i32(xq, w)
+    for layout, wl in ((1, w), (0, np.ascontiguousarray(w.T))):
+        acc = torch.empty((M, N), dtype=torch.int32, device="cuda")
+        mcv_b200.matmul_w8a8_i32(D(torch, xq), D(torch, wl), acc, w_layout=layout)
+        torch.cuda.synchronize()
+        assert np.array_equal(H(acc), ref), layout
+
+
+@pytest.mark.parametrize("layout", [0, 1])
+def test_quantize_weight_exact(cuda, layout):
+    import mcv_b200
+    torch = cuda
+    r = synth.rng(31)
+    K, N = 1024, 512
+    w = (r.standard_normal((K, N), dtype=np.float32) * 0.03).astype(np.float16)
+    w[:, 7] = 0  # all-zero column -> scale clamps to 1e-8
+    rq, rs = oracle.quantize_dense_weight_w8a8(w)
+    wq = torch.empty((N, K) if layout == 0 else (K, N), dtype=torch.int8, device="cuda")
+    sc = torch.empty(N, dtype=torch.float16, device="cuda")
+    mcv_b200.quantize_dense_weight_w8a8(D(torch, w), wq, sc, w_layout=layout)
+    torch.cuda.synchronize()
+    got = H(wq) if layout == 1 else H(wq).T
+    assert np.array_equal(got, rq)
+    assert np.array_equal(H(sc), rs)
