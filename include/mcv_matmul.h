@@ -160,6 +160,24 @@ int mcv_lm_head_argmax(const void* x, const void* w, void* out_key, void* out_in
 int mcv_argmax_last_dim_f16(const void* logits, void* out_index, int64_t M, int64_t V,
                             mcv_stream_t stream);
 
+/* mcv_lm_head_argmax without a caller workspace.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory (code
+ * running where cudaMalloc is forbidden or unwanted, e.g. a host callback or a
+ * plugin whose host owns every allocation).  Its workspace is a fixed array of
+ * mcv_lm_head_noalloc_max_bytes() bytes in the library's device memory,
+ * reserved on every GPU that loads the library until the process exits; it is
+ * large enough for every supported M (1..8), and larger requests are rejected
+ * with MCV_ERR_WORKSPACE.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress), so make that first call before any
+ * stream capture.  Each call clears the array's header with cudaMemsetAsync on
+ * `stream` and allocates nothing.  All calls share the one array: calls that
+ * may overlap on the GPU (other streams, other threads) race and must be
+ * serialised by the caller. */
+size_t mcv_lm_head_noalloc_max_bytes(void);
+int mcv_lm_head_argmax_noalloc(const void* x, const void* w, void* out_key, void* out_index,
+                               int64_t M, int64_t K, int64_t N_shard, int64_t n_offset,
+                               int fp16_logits, mcv_stream_t stream);
+
 /* int64 index[m] = 0xFFFFFFFF - (uint32)key[m]: decode argmax keys on the device. */
 int mcv_argmax_key_to_index(const void* key, void* out_index, int64_t M, mcv_stream_t stream);
 

@@ -47,6 +47,8 @@ _SIGS = {
     "mcv_lm_head_argmax": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _sz, _vp],
     "mcv_argmax_last_dim_f16": [_vp, _vp, _i64, _i64, _vp],
     "mcv_argmax_key_to_index": [_vp, _vp, _i64, _vp],
+    "mcv_lm_head_noalloc_max_bytes": [],
+    "mcv_lm_head_argmax_noalloc": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp],
     "mcv_nccl_unique_id_bytes": [],
     "mcv_nccl_get_unique_id": [_vp],
     "mcv_nccl_comm_init": [_vp, _int, _vp, _int],
@@ -64,6 +66,7 @@ _RESTYPE = {
     "mcv_set_pdl": None,
     "mcv_lm_head_workspace_size": _sz,
     "mcv_nccl_unique_id_bytes": _sz,
+    "mcv_lm_head_noalloc_max_bytes": _sz,
 }
 EXPORTED = tuple(_SIGS)
 
