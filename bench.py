@@ -172,34 +172,44 @@ def rand_f16(torch, shape, std, gen):
 
 
 def bench_w4a16_gemv(torch, mcv, synth, l2, hbm):
+    """Config 0 two ways: (a) a dependent chain, one GEMV per launch, each
+    reading x only after the previous kernel finished (decode semantics);
+    (b) independent config-0 GEMVs, 48 per grouped launch (batch
+    throughput).  Both rotate over weight copies totalling more than 2x L2."""
     M, K, N = 1, 1024, 3584
     x, q, z, s = synth.w4a16_inputs(M, K, N, seed=0)
     w0 = mcv.pack_w4a16(q, z, s)
     per = synth.w4a16_bytes(M, K, N)
-    copies = max(2, int(np.ceil(2 * l2 / w0.nbytes)))
+    copies = max(2, int(np.ceil(2 * l2 / w0.nbytes / 48)) * 48)
     ws = [w0] + [mcv.W4A16QuantizedWeight(w0.qweight.clone(), w0.scales.clone(), w0.zeros.clone(), w0.zero_bias,
                                           K, N) for _ in range(copies - 1)]
     xd = torch.from_numpy(x).cuda()
     out = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    outs = [torch.empty((M, N), dtype=torch.float16, device="cuda") for _ in range(copies)]
 
-    def step():
+    def chain():
         for w in ws:
             mcv.matmul_w4a16(xd, w, out)
-    s0 = torch.cuda.Stream()
-    step()
-    torch.cuda.synchronize()
-    g = graph_of(torch, step, s0)
-    for _ in range(3):
-        g.replay()
-    torch.cuda.synchronize()
-    ms = time_graph_ms(torch, g, reps=20) / copies
-    us = ms * 1e3
-    gbs = per / (us * 1e-6) / 1e9
-    return {"config": "config0 M=1 K=1024 N=3584 group=128", "us_per_gemv": round(us, 4),
-            "GBps": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 4), "bytes_per_gemv": per,
-            "timing": f"CUDA graph of {copies} back-to-back GEMVs over distinct weight copies "
-                      f"({copies * w0.nbytes / 1e6:.0f} MB > 2x L2), PDL on, 20 replays",
-            "gpu_launches_per_replay": copies}
+    probs = mcv.w4a16_problems([(xd, w, o) for w, o in zip(ws, outs)])
+
+    def grouped():
+        mcv.matmul_w4a16_grouped(None, problems=probs)
+    res = {"config": "config0 M=1 K=1024 N=3584 group=128", "bytes_per_gemv": per}
+    for name, fn, launches in (("chain", chain, copies), ("grouped", grouped, copies // 48)):
+        fn()
+        torch.cuda.synchronize()
+        g = graph_of(torch, fn, torch.cuda.Stream())
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        us = time_graph_ms(torch, g, reps=20) / copies * 1e3
+        gbs = per / (us * 1e-6) / 1e9
+        res[name] = {"us_per_gemv": round(us, 4), "GBps": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 4),
+                     "gpu_launches_per_replay": launches}
+    res["timing"] = (f"CUDA graph over {copies} weight copies ({copies * w0.nbytes / 1e6:.0f} MB > 2x L2), PDL on, "
+                     "20 replays; chain = one launch per GEMV, each reading x after the previous kernel; "
+                     "grouped = 48 independent GEMVs per launch")
+    return res
 
 
 def bench_w8a8(torch, mcv, synth, l2, hbm):
@@ -233,33 +243,105 @@ def bench_w8a8(torch, mcv, synth, l2, hbm):
 
 
 def bench_decode_step(torch, mcv, synth, hbm, lm_w, ws_lm):
+    """Config 3: the 186 projections of one token + the lm_head.  'separate'
+    launches each projection on its own (the reference's call pattern);
+    'grouped' launches the projections that read the same input together
+    (qkv/z/a/b, q/k/v, gate/up): 96 W4A16 launches per token."""
     shapes = synth.decode_step_shapes()
     weights = []
     for i, (_, _, K, N) in enumerate(shapes):
         _, q, z, s = synth.w4a16_inputs(1, K, N, seed=1000 + i)
         weights.append(mcv.pack_w4a16(q, z, s))
     xs = {K: torch.randn((1, K), device="cuda").to(torch.float16) for K in (1024, 2048, 3584)}
-    outs = {N: torch.empty((1, N), dtype=torch.float16, device="cuda") for _, _, _, N in shapes}
+    outs = [torch.empty((1, N), dtype=torch.float16, device="cuda") for _, _, _, N in shapes]
     idx = torch.empty(1, dtype=torch.int64, device="cuda")
     x_lm = xs[1024]
+    same_input = {"linear_qkv", "linear_z", "linear_a", "linear_b", "full_q", "full_k", "full_v", "mlp_gate", "mlp_up"}
+    groups, cur = [], []
+    for i, (layer, name, K, N) in enumerate(shapes):
+        key = (layer, "attn_in" if name.startswith(("linear_", "full_")) else "mlp_in")
+        if name in same_input and cur and cur[0][0] == key:
+            cur.append((key, i))
+            continue
+        if cur:
+            groups.append([j for _, j in cur])
+        cur = [(key, i)] if name in same_input else []
+        if name not in same_input:
+            groups.append([i])
+    if cur:
+        groups.append([j for _, j in cur])
+    probs = [mcv.w4a16_problems([(xs[shapes[i][2]], weights[i], outs[i]) for i in grp]) for grp in groups]
 
-    def step():
-        for (_, _, K, N), w in zip(shapes, weights):
-            mcv.matmul_w4a16(xs[K], w, outs[N])
+    def separate():
+        for (_, _, K, N), w, o in zip(shapes, weights, outs):
+            mcv.matmul_w4a16(xs[K], w, o)
         mcv.lm_head_argmax(x_lm, lm_w, ws_lm, out_index=idx)
-    step()
-    torch.cuda.synchronize()
-    g = graph_of(torch, step, torch.cuda.Stream())
-    for _ in range(2):
-        g.replay()
-    torch.cuda.synchronize()
-    ms = time_graph_ms(torch, g, reps=10)
+
+    def grouped():
+        for p in probs:
+            mcv.matmul_w4a16_grouped(None, problems=p)
+        mcv.lm_head_argmax(x_lm, lm_w, ws_lm, out_index=idx)
     byts = sum(synth.w4a16_bytes(1, K, N) for _, _, K, N in shapes) + VOCAB * K_HIDDEN * 2 + K_HIDDEN * 2
-    gbs = byts / (ms * 1e-3) / 1e9
-    return {"config": "config3: 186 W4A16 GEMVs (24-layer hybrid LM) + fp16 lm_head argmax, M=1",
-            "us_per_token": round(ms * 1e3, 2), "bytes_per_token": byts, "GBps": round(gbs, 1),
-            "frac_of_hbm": round(gbs / hbm, 4), "gpu_launches_per_token": len(shapes) + 1,
-            "timing": "one CUDA graph per token (PDL edges), 10 replays"}
+    res = {"config": "config3: 186 W4A16 GEMVs (24-layer hybrid LM) + fp16 lm_head argmax, M=1",
+           "bytes_per_token": byts, "roofline_us": round(byts / (hbm * 1e3), 2)}
+    for name, fn, launches in (("separate", separate, len(shapes) + 1), ("grouped", grouped, len(groups) + 1)):
+        fn()
+        torch.cuda.synchronize()
+        g = graph_of(torch, fn, torch.cuda.Stream())
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize()
+        ms = time_graph_ms(torch, g, reps=10)
+        gbs = byts / (ms * 1e-3) / 1e9
+        res[name] = {"us_per_token": round(ms * 1e3, 2), "GBps": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 4),
+                     "gpu_launches_per_token": launches}
+    res["timing"] = "one CUDA graph per token (PDL edges), 10 replays"
+    return res
+
+
+def run_profile(args):
+    """Untimed launches for an ncu capture: 2 warm-up + 3 profiled launches."""
+    import torch
+    import mcv_b200 as mcv
+    from mcv_b200 import synth
+    torch.cuda.set_device(0)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(7)
+    if args.profile == "lm_head":
+        w = rand_f16(torch, (args.rows, K_HIDDEN), 0.02, gen)
+        x = rand_f16(torch, (1, K_HIDDEN), 1.0, gen)
+        ws = mcv.lm_head_workspace(1)
+        idx = torch.empty(1, dtype=torch.int64, device="cuda")
+        for _ in range(5):
+            mcv.lm_head_argmax(x, w, ws, out_index=idx)
+    elif args.profile == "w4a16":
+        x, q, z, s = synth.w4a16_inputs(1, 1024, 3584, seed=0)
+        w = mcv.pack_w4a16(q, z, s)
+        xd = torch.from_numpy(x).cuda()
+        out = torch.empty((1, 3584), dtype=torch.float16, device="cuda")
+        for _ in range(5):
+            mcv.matmul_w4a16(xd, w, out)
+    elif args.profile == "w4a16_grouped":
+        # 48 independent config-0 GEMVs in one launch (88 MB of weights)
+        x, q, z, s = synth.w4a16_inputs(1, 1024, 3584, seed=0)
+        w0 = mcv.pack_w4a16(q, z, s)
+        ws = [w0] + [mcv.W4A16QuantizedWeight(w0.qweight.clone(), w0.scales.clone(), w0.zeros.clone(), 0, 1024, 3584)
+                     for _ in range(47)]
+        xd = torch.from_numpy(x).cuda()
+        outs = [torch.empty((1, 3584), dtype=torch.float16, device="cuda") for _ in ws]
+        probs = mcv.w4a16_problems(list(zip([xd] * 48, ws, outs)))
+        for _ in range(5):
+            mcv.matmul_w4a16_grouped(None, problems=probs)
+    elif args.profile == "w8a8":
+        for M in (1, 8):
+            x, w8, ws8 = synth.w8a8_inputs(M, 1024, 3584, seed=2)
+            wt = torch.from_numpy(np.ascontiguousarray(w8.T)).cuda()
+            out = torch.empty((M, 3584), dtype=torch.float16, device="cuda")
+            for _ in range(5):
+                mcv.w8a8_fused(torch.from_numpy(x).cuda(), wt, torch.from_numpy(ws8).cuda(), out, w_layout=0)
+    torch.cuda.synchronize()
+    print(f"profile case {args.profile} done", flush=True)
+    return 0
 
 
 def main():
@@ -269,10 +351,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="mcv", choices=["mcv", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip the config 0/2/3 sub-benchmarks")
+    ap.add_argument("--profile", choices=["lm_head", "w4a16", "w4a16_grouped", "w8a8"],
+                    help="run a few untimed launches of one kernel family (a small case for ncu)")
+    ap.add_argument("--rows", type=int, default=65536, help="--profile lm_head: vocab rows (65536 = 128 MB)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile:
+        return run_profile(args)
 
     import torch
     import mcv_b200 as mcv

@@ -61,18 +61,23 @@ void mcv_set_pdl(int enabled);
 /* W4A16: int4 weights, fp16 group scales and 4-bit zeros, fp16 activations */
 /* ======================================================================== */
 /*
- * Device weight layout "mcv-int4" (prepared once at load time):
- *   qweight  uint32 [N][K/8]    column n's K values, 8 per word.  Within a
- *                               word holding k = 8j..8j+7, the 4-bit value of
- *                               k = 8j+i sits at nibble slot {0,4,1,5,2,6,3,7}[i],
- *                               so one LOP3 per pair yields two fp16 lanes.
- *   scales   fp16   [N][G]      G = K/group, scale of (group g, column n)
- *   zeros    uint32 [N][ceil(G/8)]  4-bit zero of (g, n) at nibble g%8 of
- *                               word g/8; effective zero = nibble + zero_bias
+ * Device weight layout "mcv-int4" (prepared once at load time; group = 128,
+ * the only quantization group the reference supports, ops.h:95-103):
+ *   qweight  uint32 [Npad/16][K/64][32][4]   Npad = N rounded up to 16.
+ *            Output columns form strips of 16; per strip, groups of four
+ *            16-k blocks follow each other; entry [s][kq][l][j] is lane l's
+ *            word for k-block 4*kq+j: the eight 4-bit values lane l feeds to
+ *            one m16n8k16 tensor-core MMA as its A fragment (rows = the
+ *            strip's columns), (col, k) = (l/4, 2(l%4)), (l/4, 2(l%4)+1),
+ *            (l/4+8, 2(l%4)), (l/4+8, 2(l%4)+1), then the same at k+8, in
+ *            nibble slots 0,4,1,5,2,6,3,7.
+ *   scales   fp16   [Npad][Gpad]   G = K/128, Gpad = G rounded up to 8
+ *   zeros    uint32 [Npad][ceil(G/8)]  4-bit zero of (g, n) at nibble g%8 of
+ *            word g/8; effective zero = nibble + zero_bias
  *   zero_bias 0 for AWQ and synthetic weights, 1 for GPTQ (whose stored zero
- *             is one less than the true zero, src/csrc/lib/quantized_weight.cpp:112)
- * Dequantised weight w[k][n] = (q - zero) * scale.  Requires K % group == 0,
- * group % 32 == 0, and 16-byte aligned qweight.
+ *            is one less than the true zero, src/csrc/lib/quantized_weight.cpp:112)
+ * Padding columns and groups have q = zero = 0 and scale 0.  Dequantised
+ * weight w[k][n] = (q - zero) * scale.  K must be a multiple of 128.
  */
 
 /* Bytes of each array of the mcv-int4 layout. */
@@ -115,12 +120,33 @@ int mcv_w4a16_pack_from_tiles_host(const int8_t* packed, int64_t tile_len,
                                    uint32_t* zeros_out, int* zero_bias_out);
 
 /* out[m][n] = sum_k x[m][k] * w[k][n], M = 1..8, fp32 accumulation, fp16 out.
- * x fp16 [M][K], out fp16 [M][N].
+ * x fp16 [M][K] (4-byte aligned), out fp16 [M][N]; group must be 128;
+ * qweight and scales 16-byte aligned.
  * Replaces matmul_w4a16 (src/csrc/lib/ops.cpp:1030-1095, ops.h:95-108; M=1
  * there) and its kernel op_kernel/matmul_w4a16_custom.cpp. */
 int mcv_w4a16_gemv(const void* x, const void* qweight, const void* scales, const void* zeros,
                    int zero_bias, void* out, int64_t M, int64_t K, int64_t N, int64_t group,
                    mcv_stream_t stream);
+
+/* Several independent W4A16 GEMVs (same M) in one launch: problems is a HOST
+ * array; each entry's x/out/weights are device pointers.  No problem may read
+ * another problem's output.  For projections that share an input (q/k/v,
+ * gate/up, the linear-attention qkv/z/a/b of src/csrc/lib/decoder_layer.cpp:
+ * 1110-1114, :970-972, :1200-1201) and for batches of unrelated GEMVs.
+ * Launches ceil(count/48) kernels. */
+typedef struct mcv_w4a16_problem {
+    const void* x;
+    const void* qweight;
+    const void* scales;
+    const void* zeros;
+    void* out;
+    int32_t K;
+    int32_t N;
+    int32_t group;
+    int32_t zero_bias;
+} mcv_w4a16_problem;
+int mcv_w4a16_gemv_grouped(const mcv_w4a16_problem* problems, int count, int64_t M,
+                           mcv_stream_t stream);
 
 /* ======================================================================== */
 /* dense fp16 GEMV and the lm_head                                          */

@@ -3,24 +3,32 @@
 //
 // Reference behaviour replaced: matmul_w4a16 (src/csrc/lib/ops.cpp:1030-1095)
 // and its AscendC kernel op_kernel/matmul_w4a16_custom.cpp:64-127, which
-// computes out[n] = sum_g s[g,n] * sum_{k in g} x[k] * (q-z)[k,n] on 8 AICore
-// blocks with fp16 accumulation.  Here the same sum is accumulated in fp32.
+// computes out[n] = sum_g s[g,n] * sum_{k in g} x[k] * (q-z)[k,n] (group 128)
+// on 8 AICore blocks with fp16 accumulation.  Here every group's partial sum
+// is accumulated in fp32 and scaled in fp32.
 //
-// Kernel design (HBM-bound; a 1024x3584 weight is 1.84 MB of int4):
-//  * one warp owns CPW output columns; lane l streams 16-byte chunks
-//    (32 consecutive k of one column) c = l, l+32, ... so each warp-wide load
-//    instruction reads 512 contiguous bytes;
-//  * every weight, scale and zero load of the thread is issued up front,
-//    before griddepcontrol.wait, so under programmatic dependent launch the
-//    weight stream of this GEMV overlaps the previous kernel's tail;
-//  * int4 -> fp16 with the exponent-bias ("magic number") conversion
+// Design (HBM-bound: a 1024x3584 weight is 1.84 MB of int4):
+//  * Layout.  Output columns form strips of 16.  A strip's weights are stored
+//    k-block (16 k) after k-block, four k-blocks per 16-byte lane vector, and
+//    lane l's 32-bit word of a k-block holds exactly the eight 4-bit values it
+//    feeds to one m16n8k16 tensor-core MMA as its A fragment (rows = the 16
+//    columns of the strip).  So one coalesced 16-byte load per lane brings the
+//    fragments of four MMAs, and a warp-wide load reads 512 contiguous bytes.
+//  * Work.  A persistent grid; each warp owns whole strips (all of K) and
+//    walks them in chunks of 512 k: the next chunk's eight 16-byte loads per
+//    lane are issued before the current chunk is computed (register double
+//    buffering, ~64 KB per SM in flight).  The first chunk is loaded before
+//    griddepcontrol.wait, so under programmatic dependent launch the weight
+//    stream overlaps the previous kernel.
+//  * Math.  int4 -> fp16 by the exponent-bias ("magic number") conversion
 //    described for FasterTransformer-style mixed-input GEMMs (Kim et al.,
 //    "Who Says Elephants Can't Run", 2022; Frantar et al., MARLIN, 2024):
 //    OR-ing a nibble into the mantissa of fp16 1024.0 gives 1024+q exactly,
-//    and one HSUB2 / HFMA2 removes 1024+zero, leaving (q - zero) exactly;
-//  * products are accumulated in fp32 by the sm_100 mixed-precision FMA
-//    (fp16 x fp16 + fp32), per 32-weight chunk, then scaled by the group
-//    scale; a 5-step xor-shuffle reduces over the warp.
+//    and one HSUB2/HFMA2 leaves (q - zero) exactly.  mma.sync m16n8k16 with
+//    fp32 accumulation multiplies them by x (B operand, up to 8 rows); each
+//    128-k group gets fresh accumulators that are scaled in fp32 and added to
+//    the running sums.  The MMA is used here to keep the ALU instruction
+//    count per weight low (~1.3) in an HBM-bound kernel, not for its FLOPs.
 #include <algorithm>
 #include <cstring>
 #include <vector>
@@ -30,164 +38,264 @@
 namespace mcv {
 namespace {
 
-constexpr int kWarps = 4;
-constexpr int kCpw = 2;  // columns per warp
-constexpr int kSlot[8] = {0, 4, 1, 5, 2, 6, 3, 7};
+constexpr int kGroup = 128;        // quantization group along K (the reference's only size)
+constexpr int kChunkK = 512;       // k per register buffer (8 lane vectors, 4 groups)
+constexpr int kWarps = 8;
+constexpr int kBlocksPerSm = 2;
+constexpr int kMaxGroupProblems = 48;
 
-// Four half2 values (q - z) for k = 8j..8j+7 of one word (see kSlot).
-__device__ __forceinline__ void dequant8(uint32_t w, __half2 zlo, __half2 zhi, uint32_t h[4]) {
-    constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024.0 in both lanes
-    const __half2 inv16 = __halves2half2(__ushort_as_half(0x2c00), __ushort_as_half(0x2c00));
-    const uint32_t w8 = w >> 8;
-    const __half2 a = u32_as_h2(lop3_and_or(w, 0x000f000fu, kMagic));
-    const __half2 b = u32_as_h2(lop3_and_or(w, 0x00f000f0u, kMagic));
-    const __half2 c = u32_as_h2(lop3_and_or(w8, 0x000f000fu, kMagic));
-    const __half2 d = u32_as_h2(lop3_and_or(w8, 0x00f000f0u, kMagic));
-    h[0] = h2_as_u32(__hsub2(a, zlo));
-    h[1] = h2_as_u32(__hfma2(b, inv16, zhi));
-    h[2] = h2_as_u32(__hsub2(c, zlo));
-    h[3] = h2_as_u32(__hfma2(d, inv16, zhi));
+inline int64_t padded_n(int64_t N) { return (N + 15) / 16 * 16; }
+inline int64_t padded_g(int64_t G) { return (G + 7) / 8 * 8; }
+
+// Fragment element e of lane (g = lane/4, t = lane%4):
+// (row, k) = (g, 2t), (g, 2t+1), (g+8, 2t), (g+8, 2t+1), then the same at k+8.
+// Nibble slots are chosen so that LOP3 with 0x000F000F / 0x00F000F0 on the
+// word and on word >> 8 yields the four half2 registers a0..a3 in order.
+constexpr int kFragSlot[8] = {0, 4, 1, 5, 2, 6, 3, 7};
+constexpr int kFragRow[8] = {0, 0, 8, 8, 0, 0, 8, 8};
+constexpr int kFragK[8] = {0, 1, 0, 1, 8, 9, 8, 9};
+
+struct Problem {
+    const __half* x;
+    const uint4* qw;
+    const __half* s;   // [Npad][Gpad8]
+    const uint32_t* z; // [Npad][ceil(G/8)]
+    __half* out;
+    int K, N, zero_bias;
+    int strip_begin;   // first global strip index of this problem
+};
+
+struct GroupParams {
+    int count;
+    int total_strips;
+    Problem p[kMaxGroupProblems];
+};
+
+__device__ __forceinline__ void mma_16816(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-template <int M, int KCH>
-__global__ void __launch_bounds__(kWarps * 32)
-w4a16_gemv_kernel(const __half* __restrict__ x, const uint32_t* __restrict__ qw,
-                  const __half* __restrict__ scales, const uint32_t* __restrict__ zeros,
-                  int zero_bias, __half* __restrict__ out, int K, int N, int group) {
-    const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
-    const int n0 = (blockIdx.x * kWarps + warp) * kCpw;
-    const int chunks = K >> 5;
-    const int kwords = K >> 3;
-    const int G = K / group;
-    const int zwords = (G + 7) >> 3;
+__device__ __forceinline__ int find_problem(const GroupParams& gp, int strip, int start) {
+    int pi = start;
+    while (pi + 1 < gp.count && strip >= gp.p[pi + 1].strip_begin) ++pi;
+    return pi;
+}
 
-    // ---- prefetch everything that does not depend on the previous kernel ----
-    uint4 wv[kCpw][KCH];
-    float sc[kCpw][KCH];
-    int zq[kCpw][KCH];
+// Register buffer of one (strip, 512-k chunk): eight lane vectors (32
+// k-blocks), the scales of the chunk's 4 groups for the lane's two columns
+// (rows g and g+8 of the MMA) and their zero nibbles.
+struct Chunk {
+    uint4 w[8];
+    uint2 slo, shi;
+    uint32_t zlo, zhi;
+};
+
+__device__ __forceinline__ void load_chunk(Chunk& b, const Problem& P, int sl, int c, int lane) {
+    const int K = P.K, G = K / kGroup, Gp = (G + 7) & ~7, zw = (G + 7) >> 3;
+    const int nq = min(8, (K - c * kChunkK) / 64);  // lane vectors in this chunk
+    const size_t base = (static_cast<size_t>(sl) * (K / 64) + c * 8) * 32 + lane;
 #pragma unroll
-    for (int j = 0; j < kCpw; ++j) {
-        const int n = n0 + j;
+    for (int q = 0; q < 8; ++q) b.w[q] = q < nq ? ld_stream(P.qw + base + q * 32) : make_uint4(0, 0, 0, 0);
+    const int col = sl * 16 + (lane >> 2);
+    b.slo = *reinterpret_cast<const uint2*>(P.s + static_cast<size_t>(col) * Gp + c * 4);
+    b.shi = *reinterpret_cast<const uint2*>(P.s + static_cast<size_t>(col + 8) * Gp + c * 4);
+    const int sh = 16 * (c & 1);
+    b.zlo = P.z[static_cast<size_t>(col) * zw + (c >> 1)] >> sh;
+    b.zhi = P.z[static_cast<size_t>(col + 8) * zw + (c >> 1)] >> sh;
+}
+
+__device__ __forceinline__ float half_of(uint2 v, int i) {
+    const uint32_t w = (i < 2) ? v.x : v.y;
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> (16 * (i & 1)))));
+}
+
+// Computes one chunk into acc (rows g / g+8, columns 2t / 2t+1 of the MMA
+// output tile = output columns n0+g, n0+g+8 of activation rows 2t, 2t+1).
+template <int M>
+__device__ __forceinline__ void compute_chunk(const Chunk& b, const Problem& P, int c, int lane, float acc[4]) {
+    const int K = P.K;
+    const int nq = min(8, (K - c * kChunkK) / 64);
+    const int g = lane >> 2, t = lane & 3;
+    const __half* xrow = P.x + static_cast<size_t>(g) * K + c * kChunkK + 2 * t;
+    const __half2 inv16 = __halves2half2(__ushort_as_half(0x2c00), __ushort_as_half(0x2c00));
 #pragma unroll
-        for (int i = 0; i < KCH; ++i) {
-            const int c = lane + 32 * i;
-            wv[j][i] = make_uint4(0, 0, 0, 0);
-            sc[j][i] = 0.0f;
-            zq[j][i] = 0;
-            if (n < N && c < chunks) {
-                wv[j][i] = ld_stream(qw + static_cast<size_t>(n) * kwords + c * 4);
-                const int g = (c * 32) / group;
-                sc[j][i] = __half2float(scales[static_cast<size_t>(n) * G + g]);
-                const uint32_t zw = zeros[static_cast<size_t>(n) * zwords + (g >> 3)];
-                zq[j][i] = static_cast<int>((zw >> (4 * (g & 7))) & 0xfu) + zero_bias;
+    for (int gi = 0; gi < 4; ++gi) {
+        if (2 * gi >= nq) break;
+        uint32_t bx[8][2];
+#pragma unroll
+        for (int kb = 0; kb < 8; ++kb) {
+            bx[kb][0] = bx[kb][1] = 0u;
+            if (g < M) {
+                const __half* p = xrow + gi * kGroup + kb * 16;
+                bx[kb][0] = *reinterpret_cast<const uint32_t*>(p);
+                bx[kb][1] = *reinterpret_cast<const uint32_t*>(p + 8);
             }
         }
+        const int zl_q = static_cast<int>((b.zlo >> (4 * gi)) & 0xfu) + P.zero_bias;
+        const int zh_q = static_cast<int>((b.zhi >> (4 * gi)) & 0xfu) + P.zero_bias;
+        const __half z1 = __int2half_rn(1024 + zl_q);   // rows g: 1024 + zero
+        const __half z2 = __int2half_rn(-(64 + zh_q));  // rows g+8: -(64 + zero)
+        const __half2 zl = __halves2half2(z1, z1);
+        const __half2 zh = __halves2half2(z2, z2);
+        float e[4] = {0.0f, 0.0f, 0.0f, 0.0f}, o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int kb = 0; kb < 8; ++kb) {
+            const uint4 v = b.w[2 * gi + (kb >> 2)];
+            const uint32_t w = (kb & 3) == 0 ? v.x : (kb & 3) == 1 ? v.y : (kb & 3) == 2 ? v.z : v.w;
+            const uint32_t w8 = w >> 8;
+            constexpr uint32_t kMagic = 0x64006400u;
+            uint32_t a[4];
+            a[0] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w, 0x000f000fu, kMagic)), zl));
+            a[1] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w, 0x00f000f0u, kMagic)), inv16, zh));
+            a[2] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w8, 0x000f000fu, kMagic)), zl));
+            a[3] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w8, 0x00f000f0u, kMagic)), inv16, zh));
+            if (kb & 1) mma_16816(o, a, bx[kb][0], bx[kb][1]);
+            else mma_16816(e, a, bx[kb][0], bx[kb][1]);
+        }
+        const float s_lo = half_of(b.slo, gi), s_hi = half_of(b.shi, gi);
+        acc[0] = fmaf(e[0] + o[0], s_lo, acc[0]);
+        acc[1] = fmaf(e[1] + o[1], s_lo, acc[1]);
+        acc[2] = fmaf(e[2] + o[2], s_hi, acc[2]);
+        acc[3] = fmaf(e[3] + o[3], s_hi, acc[3]);
     }
-    pdl_trigger();
-    pdl_wait();
-
-    float acc[kCpw][M];
-#pragma unroll
-    for (int j = 0; j < kCpw; ++j)
-#pragma unroll
-        for (int m = 0; m < M; ++m) acc[j][m] = 0.0f;
-
-#pragma unroll
-    for (int i = 0; i < KCH; ++i) {
-        const int c = lane + 32 * i;
-        if (c >= chunks) break;
-        float pa[kCpw][M], pb[kCpw][M];
-#pragma unroll
-        for (int j = 0; j < kCpw; ++j)
-#pragma unroll
-            for (int m = 0; m < M; ++m) pa[j][m] = pb[j][m] = 0.0f;
-        __half2 zlo[kCpw], zhi[kCpw];
-#pragma unroll
-        for (int j = 0; j < kCpw; ++j) {
-            const __half z1 = __int2half_rn(1024 + zq[j][i]);
-            const __half z2 = __int2half_rn(-(64 + zq[j][i]));
-            zlo[j] = __halves2half2(z1, z1);
-            zhi[j] = __halves2half2(z2, z2);
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            uint4 xv[M];
-#pragma unroll
-            for (int m = 0; m < M; ++m)
-                xv[m] = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(m) * K + c * 32 + q * 8);
-#pragma unroll
-            for (int j = 0; j < kCpw; ++j) {
-                const uint32_t w = q == 0 ? wv[j][i].x : q == 1 ? wv[j][i].y : q == 2 ? wv[j][i].z : wv[j][i].w;
-                uint32_t h[4];
-                dequant8(w, zlo[j], zhi[j], h);
-#pragma unroll
-                for (int m = 0; m < M; ++m) {
-                    fma2_f16_f32(pa[j][m], pb[j][m], h[0], xv[m].x);
-                    fma2_f16_f32(pa[j][m], pb[j][m], h[1], xv[m].y);
-                    fma2_f16_f32(pa[j][m], pb[j][m], h[2], xv[m].z);
-                    fma2_f16_f32(pa[j][m], pb[j][m], h[3], xv[m].w);
-                }
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < kCpw; ++j)
-#pragma unroll
-            for (int m = 0; m < M; ++m) acc[j][m] = fmaf(pa[j][m] + pb[j][m], sc[j][i], acc[j][m]);
-    }
-
-#pragma unroll
-    for (int j = 0; j < kCpw; ++j)
-#pragma unroll
-        for (int m = 0; m < M; ++m) {
-            const float v = warp_sum(acc[j][m]);
-            const int n = n0 + j;
-            if (lane == ((j * M + m) & 31) && n < N)
-                out[static_cast<size_t>(m) * N + n] = __float2half_rn(v);
-        }
 }
 
 template <int M>
-int dispatch_k(int kch, const __half* x, const uint32_t* qw, const __half* s, const uint32_t* z,
-               int zb, __half* out, int K, int N, int group, cudaStream_t st) {
-    const dim3 grid((N + kWarps * kCpw - 1) / (kWarps * kCpw));
-    const dim3 block(kWarps * 32);
-    switch (kch) {
-        case 1: return launch(w4a16_gemv_kernel<M, 1>, grid, block, 0, st, x, qw, s, z, zb, out, K, N, group);
-        case 2: return launch(w4a16_gemv_kernel<M, 2>, grid, block, 0, st, x, qw, s, z, zb, out, K, N, group);
-        case 4: return launch(w4a16_gemv_kernel<M, 4>, grid, block, 0, st, x, qw, s, z, zb, out, K, N, group);
-        case 8: return launch(w4a16_gemv_kernel<M, 8>, grid, block, 0, st, x, qw, s, z, zb, out, K, N, group);
-        default: return fail(MCV_ERR_SHAPE, "w4a16_gemv: K above 8192 unsupported");
+__device__ __forceinline__ void store_strip(const Problem& P, int sl, int lane, const float acc[4]) {
+    const int g = lane >> 2, t = lane & 3;
+    const int n0 = sl * 16;
+    const size_t N = static_cast<size_t>(P.N);
+    const int m0 = 2 * t;
+    if (m0 < M) {
+        if (n0 + g < P.N) P.out[m0 * N + n0 + g] = __float2half_rn(acc[0]);
+        if (n0 + g + 8 < P.N) P.out[m0 * N + n0 + g + 8] = __float2half_rn(acc[2]);
+    }
+    if (m0 + 1 < M) {
+        if (n0 + g < P.N) P.out[(m0 + 1) * N + n0 + g] = __float2half_rn(acc[1]);
+        if (n0 + g + 8 < P.N) P.out[(m0 + 1) * N + n0 + g + 8] = __float2half_rn(acc[3]);
+    }
+}
+
+// Warp w of block b is global warp (w * gridDim.x + b), so consecutive strips
+// land on different SMs first; it owns strips gw, gw + W, gw + 2W, ...
+template <int M>
+__global__ void __launch_bounds__(kWarps * 32, kBlocksPerSm)
+w4a16_gemv_kernel(const __grid_constant__ GroupParams gp) {
+    const int lane = threadIdx.x & 31;
+    const int W = static_cast<int>(gridDim.x) * kWarps;
+    int strip = (threadIdx.x >> 5) * static_cast<int>(gridDim.x) + static_cast<int>(blockIdx.x);
+    const int T = gp.total_strips;
+    Chunk A, B;  // two named buffers: a dynamically indexed pair would live in local memory
+    int pi = 0, c = 0;
+    if (strip < T) {
+        pi = find_problem(gp, strip, 0);
+        load_chunk(A, gp.p[pi], strip - gp.p[pi].strip_begin, 0, lane);
+    }
+    pdl_trigger();
+    pdl_wait();  // x may be the previous kernel's output
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    // one step: prefetch the (strip, chunk) after the current one into nb,
+    // compute the current one from cb
+    auto step = [&](Chunk& cb, Chunk& nb) {
+        const Problem& P = gp.p[pi];
+        const int nchunks = (P.K + kChunkK - 1) / kChunkK;
+        int ns = strip, nc = c + 1, npi = pi;
+        if (nc == nchunks) {
+            ns = strip + W;
+            nc = 0;
+        }
+        if (ns < T) {
+            npi = find_problem(gp, ns, pi);
+            load_chunk(nb, gp.p[npi], ns - gp.p[npi].strip_begin, nc, lane);
+        }
+        compute_chunk<M>(cb, P, c, lane, acc);
+        if (nc == 0) {
+            store_strip<M>(P, strip - P.strip_begin, lane, acc);
+            acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
+        }
+        strip = ns;
+        c = nc;
+        pi = npi;
+    };
+#pragma unroll 1
+    while (strip < T) {
+        step(A, B);
+        if (strip >= T) break;
+        step(B, A);
+    }
+}
+
+int assign_strips(GroupParams& gp) {
+    int t = 0;
+    for (int i = 0; i < gp.count; ++i) {
+        gp.p[i].strip_begin = t;
+        t += static_cast<int>(padded_n(gp.p[i].N) / 16);
+    }
+    gp.total_strips = t;
+    return t;
+}
+
+template <int M>
+int launch_m(GroupParams& gp, cudaStream_t st) {
+    const int strips = assign_strips(gp);
+    // spread strips over SMs first; at most kBlocksPerSm resident blocks per SM
+    const int blocks = std::min(strips, sm_count() * kBlocksPerSm);
+    return launch(w4a16_gemv_kernel<M>, dim3(blocks), dim3(kWarps * 32), 0, st, gp);
+}
+
+int run_group(GroupParams& gp, int64_t M, cudaStream_t st) {
+    switch (M) {
+        case 1: return launch_m<1>(gp, st);
+        case 2: return launch_m<2>(gp, st);
+        case 3: return launch_m<3>(gp, st);
+        case 4: return launch_m<4>(gp, st);
+        case 5: return launch_m<5>(gp, st);
+        case 6: return launch_m<6>(gp, st);
+        case 7: return launch_m<7>(gp, st);
+        default: return launch_m<8>(gp, st);
     }
 }
 
 int check_layout_dims(int64_t K, int64_t N, int64_t group) {
     if (K <= 0 || N <= 0 || group <= 0) return fail(MCV_ERR_SHAPE, "w4a16: K, N, group must be positive");
-    if (group % 32 != 0) return fail(MCV_ERR_SHAPE, "w4a16: group must be a multiple of 32");
-    if (K % group != 0) return fail(MCV_ERR_SHAPE, "w4a16: K must be a multiple of group");
-    if (K > (1 << 24) || N > (1 << 30)) return fail(MCV_ERR_SHAPE, "w4a16: dimension too large");
+    if (group != kGroup) return fail(MCV_ERR_SHAPE, "w4a16: group size must be 128 (as in the reference)");
+    if (K % group != 0) return fail(MCV_ERR_SHAPE, "w4a16: K must be a multiple of 128");
+    if (K > (1 << 20) || N > (1 << 28)) return fail(MCV_ERR_SHAPE, "w4a16: dimension too large");
     return MCV_OK;
 }
 
 // Writes the three mcv-int4 arrays from a logical accessor q(k,n) (0..15)
-// and zero z(g,n) (0..15).
+// and zero z(g,n) (0..15); padding columns get q = z = 0 and scale 0.
 template <typename QF, typename ZF>
 void pack_layout(QF q, ZF z, const uint16_t* scales_gn, int64_t K, int64_t N, int64_t group,
                  uint32_t* qw, uint16_t* sc, uint32_t* zw) {
-    const int64_t G = K / group;
-    const int64_t kwords = K / 8;
+    const int64_t G = K / group, Gp = padded_g(G), Np = padded_n(N), KQ = K / 64;
     const int64_t zwords = (G + 7) / 8;
-    for (int64_t n = 0; n < N; ++n) {
-        for (int64_t j = 0; j < kwords; ++j) {
-            uint32_t word = 0;
-            for (int i = 0; i < 8; ++i)
-                word |= (static_cast<uint32_t>(q(8 * j + i, n)) & 0xfu) << (4 * kSlot[i]);
-            qw[n * kwords + j] = word;
-        }
-        for (int64_t g = 0; g < G; ++g) sc[n * G + g] = scales_gn[g * N + n];
+    for (int64_t strip = 0; strip < Np / 16; ++strip)
+        for (int64_t kq = 0; kq < KQ; ++kq)
+            for (int lane = 0; lane < 32; ++lane)
+                for (int j = 0; j < 4; ++j) {  // k-block 4*kq + j -> component j of the lane vector
+                    const int64_t kb = kq * 4 + j;
+                    const int gg = lane >> 2, t = lane & 3;
+                    uint32_t word = 0;
+                    for (int e = 0; e < 8; ++e) {
+                        const int64_t n = strip * 16 + gg + kFragRow[e];
+                        const int64_t k = kb * 16 + 2 * t + kFragK[e];
+                        const uint32_t v = n < N ? (static_cast<uint32_t>(q(k, n)) & 0xfu) : 0u;
+                        word |= v << (4 * kFragSlot[e]);
+                    }
+                    qw[((strip * KQ + kq) * 32 + lane) * 4 + j] = word;
+                }
+    for (int64_t n = 0; n < Np; ++n) {
+        for (int64_t g = 0; g < Gp; ++g) sc[n * Gp + g] = (n < N && g < G) ? scales_gn[g * N + n] : 0;
         for (int64_t t = 0; t < zwords; ++t) zw[n * zwords + t] = 0;
-        for (int64_t g = 0; g < G; ++g)
-            zw[n * zwords + g / 8] |= (static_cast<uint32_t>(z(g, n)) & 0xfu) << (4 * (g % 8));
+        if (n < N)
+            for (int64_t g = 0; g < G; ++g)
+                zw[n * zwords + g / 8] |= (static_cast<uint32_t>(z(g, n)) & 0xfu) << (4 * (g % 8));
     }
 }
 
@@ -201,10 +309,10 @@ extern "C" {
 int mcv_w4a16_layout_bytes(int64_t K, int64_t N, int64_t group, size_t* qb, size_t* sb, size_t* zb) {
     int st = check_layout_dims(K, N, group);
     if (st) return st;
-    const int64_t G = K / group;
-    if (qb) *qb = static_cast<size_t>(N) * (K / 8) * 4;
-    if (sb) *sb = static_cast<size_t>(N) * G * 2;
-    if (zb) *zb = static_cast<size_t>(N) * ((G + 7) / 8) * 4;
+    const int64_t G = K / group, Np = padded_n(N);
+    if (qb) *qb = static_cast<size_t>(Np) * (K / 8) * 4;
+    if (sb) *sb = static_cast<size_t>(Np) * padded_g(G) * 2;
+    if (zb) *zb = static_cast<size_t>(Np) * ((G + 7) / 8) * 4;
     return MCV_OK;
 }
 
@@ -318,32 +426,40 @@ int mcv_w4a16_pack_from_tiles_host(const int8_t* packed, int64_t tile_len, const
 int mcv_w4a16_gemv(const void* x, const void* qweight, const void* scales, const void* zeros,
                    int zero_bias, void* out, int64_t M, int64_t K, int64_t N, int64_t group,
                    mcv_stream_t stream) {
-    if (!x || !qweight || !scales || !zeros || !out) return fail(MCV_ERR_NULL, "w4a16_gemv: null pointer");
-    int st = check_layout_dims(K, N, group);
-    if (st) return st;
+    if (K > (1 << 20) || N > (1 << 28)) return fail(MCV_ERR_SHAPE, "w4a16: dimension too large");
+    mcv_w4a16_problem p{x, qweight, scales, zeros, out, static_cast<int32_t>(K), static_cast<int32_t>(N),
+                        static_cast<int32_t>(group), zero_bias};
+    return mcv_w4a16_gemv_grouped(&p, 1, M, stream);
+}
+
+int mcv_w4a16_gemv_grouped(const mcv_w4a16_problem* problems, int count, int64_t M, mcv_stream_t stream) {
+    if (!problems || count < 1) return fail(MCV_ERR_NULL, "w4a16_gemv: no problems");
     if (M < 1 || M > 8) return fail(MCV_ERR_SHAPE, "w4a16_gemv: M must be 1..8");
-    if (!aligned16(qweight) || !aligned16(x)) return fail(MCV_ERR_ALIGN, "w4a16_gemv: x and qweight must be 16-byte aligned");
-    if (zero_bias < 0 || zero_bias > 1) return fail(MCV_ERR_VALUE, "w4a16_gemv: zero_bias must be 0 or 1");
-    const int chunks_per_lane = static_cast<int>((K / 32 + 31) / 32);
-    int kch = 1;
-    while (kch < chunks_per_lane) kch *= 2;
-    auto* xs = static_cast<const __half*>(x);
-    auto* qw = static_cast<const uint32_t*>(qweight);
-    auto* sc = static_cast<const __half*>(scales);
-    auto* zw = static_cast<const uint32_t*>(zeros);
-    auto* o = static_cast<__half*>(out);
-    auto s = static_cast<cudaStream_t>(stream);
-    const int k = static_cast<int>(K), n = static_cast<int>(N), g = static_cast<int>(group);
-    switch (M) {
-        case 1: return dispatch_k<1>(kch, xs, qw, sc, zw, zero_bias, o, k, n, g, s);
-        case 2: return dispatch_k<2>(kch, xs, qw, sc, zw, zero_bias, o, k, n, g, s);
-        case 3: return dispatch_k<3>(kch, xs, qw, sc, zw, zero_bias, o, k, n, g, s);
-        case 4: return dispatch_k<4>(kch, xs, qw, sc, zw, zero_bias, o, k, n, g, s);
-        case 5: return dispatch_k<5>(kch, xs, qw, sc, zw, zero_bias, o, k, n, g, s);
-        case 6: return dispatch_k<6>(kch, xs, qw, sc, zw, zero_bias, o, k, n, g, s);
-        case 7: return dispatch_k<7>(kch, xs, qw, sc, zw, zero_bias, o, k, n, g, s);
-        default: return dispatch_k<8>(kch, xs, qw, sc, zw, zero_bias, o, k, n, g, s);
+    for (int i = 0; i < count; ++i) {
+        const mcv_w4a16_problem& p = problems[i];
+        if (!p.x || !p.qweight || !p.scales || !p.zeros || !p.out) return fail(MCV_ERR_NULL, "w4a16_gemv: null pointer");
+        int st = check_layout_dims(p.K, p.N, p.group);
+        if (st) return st;
+        if (!aligned16(p.qweight) || !aligned16(p.scales))
+            return fail(MCV_ERR_ALIGN, "w4a16_gemv: qweight and scales must be 16-byte aligned");
+        if ((reinterpret_cast<uintptr_t>(p.x) | reinterpret_cast<uintptr_t>(p.zeros)) & 3u)
+            return fail(MCV_ERR_ALIGN, "w4a16_gemv: x and zeros must be 4-byte aligned");
+        if (p.zero_bias < 0 || p.zero_bias > 1) return fail(MCV_ERR_VALUE, "w4a16_gemv: zero_bias must be 0 or 1");
     }
+    auto st = static_cast<cudaStream_t>(stream);
+    for (int base = 0; base < count; base += kMaxGroupProblems) {
+        GroupParams gp{};
+        gp.count = std::min(kMaxGroupProblems, count - base);
+        for (int i = 0; i < gp.count; ++i) {
+            const mcv_w4a16_problem& q = problems[base + i];
+            gp.p[i] = Problem{static_cast<const __half*>(q.x), static_cast<const uint4*>(q.qweight),
+                              static_cast<const __half*>(q.scales), static_cast<const uint32_t*>(q.zeros),
+                              static_cast<__half*>(q.out), q.K, q.N, q.zero_bias, 0};
+        }
+        int rc = run_group(gp, M, st);
+        if (rc) return rc;
+    }
+    return MCV_OK;
 }
 
 }  // extern "C"

@@ -89,7 +89,6 @@ template <int M, int KCH, bool FUSED>
 __global__ void __launch_bounds__(kW8Warps * 32)
 w8_rows_kernel(W8Args a) {
     extern __shared__ uint4 xq_s[];  // int8 x as [M][K/16] 16-byte chunks
-    __shared__ float red[kW8Warps];
     __shared__ float xscale_s[M];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -117,23 +116,77 @@ w8_rows_kernel(W8Args a) {
 
     int8_t* xq8 = reinterpret_cast<int8_t*>(xq_s);
     if constexpr (FUSED) {
-        const __half* xh = static_cast<const __half*>(a.x);
-#pragma unroll 1
-        for (int m = 0; m < M; ++m) {
-            float mx = 0.0f;
-            for (int i = threadIdx.x; i < a.K; i += kW8Warps * 32)
-                mx = fmaxf(mx, fabsf(__half2float(xh[static_cast<int64_t>(m) * a.K + i])));
-            const float scale = scale_from_absmax(block_max_nonneg(mx, red));
-            const float inv = __fdiv_rn(1.0f, scale);
-            for (int i = threadIdx.x; i < a.K; i += kW8Warps * 32) {
-                const int8_t q = quant_act(__half2float(xh[static_cast<int64_t>(m) * a.K + i]), inv);
-                xq8[m * a.K + i] = q;
-                if (blockIdx.x == 0 && a.xq_out) a.xq_out[static_cast<int64_t>(m) * a.K + i] = q;
+        // All M rows are loaded into registers with independent 16-byte loads
+        // (one L2 round trip), reduced to per-row maxima, then quantized from
+        // the same registers into shared memory.
+        constexpr int T = kW8Warps * 32;
+        constexpr int VPT = (KCH + 3) / 4;  // 16-byte x vectors per thread per row (K <= 512*KCH)
+        const uint4* xh4 = static_cast<const uint4*>(a.x);
+        const int vpr = a.K >> 3;  // 16-byte vectors per row
+        uint4 xr[M][VPT];
+        float mx[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+#pragma unroll
+            for (int t = 0; t < VPT; ++t) {
+                const int v = threadIdx.x + t * T;
+                xr[m][t] = v < vpr ? xh4[m * vpr + v] : make_uint4(0, 0, 0, 0);
             }
-            if (threadIdx.x == 0) {
-                const __half sh = __float2half_rn(scale);
-                xscale_s[m] = __half2float(sh);
-                if (blockIdx.x == 0 && a.xs_out) a.xs_out[m] = sh;
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            mx[m] = 0.0f;
+#pragma unroll
+            for (int t = 0; t < VPT; ++t) {
+                const uint32_t wd[4] = {xr[m][t].x, xr[m][t].y, xr[m][t].z, xr[m][t].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __half22float2(u32_as_h2(wd[e]));
+                    mx[m] = fmaxf(mx[m], fmaxf(fabsf(f.x), fabsf(f.y)));
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], o));
+        __shared__ float red_m[kW8Warps][M];
+        __shared__ float inv_s[M];
+        if (lane == 0) {
+#pragma unroll
+            for (int m = 0; m < M; ++m) red_m[warp][m] = mx[m];
+        }
+        __syncthreads();
+        if (threadIdx.x < M) {
+            const int m = threadIdx.x;
+            float r = 0.0f;
+            for (int i = 0; i < kW8Warps; ++i) r = fmaxf(r, red_m[i][m]);
+            const float scale = scale_from_absmax(r);
+            inv_s[m] = __fdiv_rn(1.0f, scale);
+            const __half sh = __float2half_rn(scale);
+            xscale_s[m] = __half2float(sh);
+            if (blockIdx.x == 0 && a.xs_out) a.xs_out[m] = sh;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            const float inv = inv_s[m];
+#pragma unroll
+            for (int t = 0; t < VPT; ++t) {
+                const int v = threadIdx.x + t * T;
+                if (v >= vpr) continue;
+                const uint32_t wd[4] = {xr[m][t].x, xr[m][t].y, xr[m][t].z, xr[m][t].w};
+                uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __half22float2(u32_as_h2(wd[e]));
+                    const uint32_t q0 = static_cast<uint8_t>(quant_act(f.x, inv));
+                    const uint32_t q1 = static_cast<uint8_t>(quant_act(f.y, inv));
+                    packed[e >> 1] |= (q0 | (q1 << 8)) << (16 * (e & 1));
+                }
+                *reinterpret_cast<uint2*>(xq8 + m * a.K + v * 8) = make_uint2(packed[0], packed[1]);
+                if (blockIdx.x == 0 && a.xq_out)
+                    *reinterpret_cast<uint2*>(a.xq_out + static_cast<int64_t>(m) * a.K + v * 8) =
+                        make_uint2(packed[0], packed[1]);
             }
         }
     } else {
@@ -342,7 +395,7 @@ int launch_w8_rows_m(const W8Args& a, cudaStream_t s) {
         case 2: return go(w8_rows_kernel<M, 2, FUSED>);
         case 4: return go(w8_rows_kernel<M, 4, FUSED>);
         case 8: return go(w8_rows_kernel<M, 8, FUSED>);
-        default: return fail(MCV_ERR_SHAPE, "w8a8: K above 16384 unsupported");
+        default: return fail(MCV_ERR_SHAPE, "w8a8: K above 4096 unsupported on the [N][K] path");
     }
 }
 
@@ -449,7 +502,8 @@ int mcv_w8a8_fused(const void* x, const void* w_int8, const void* w_scale, void*
     if (st) return st;
     auto s = static_cast<cudaStream_t>(stream);
     if (w_layout == 0) {
-        if (!aligned16(w_int8)) return fail(MCV_ERR_ALIGN, "w8a8_fused: w must be 16-byte aligned");
+        if (!aligned16(w_int8) || !aligned16(x)) return fail(MCV_ERR_ALIGN, "w8a8_fused: x and w must be 16-byte aligned");
+        if (reinterpret_cast<uintptr_t>(x_int8_out) & 7u) return fail(MCV_ERR_ALIGN, "w8a8_fused: x_int8_out must be 8-byte aligned");
         W8Args a{};
         a.x = x;
         a.w = static_cast<const int8_t*>(w_int8);

@@ -42,6 +42,7 @@ _SIGS = {
     "mcv_w4a16_pack_awq_host": [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp],
     "mcv_w4a16_pack_from_tiles_host": [_vp, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _vp],
     "mcv_w4a16_gemv": [_vp, _vp, _vp, _vp, _int, _vp, _i64, _i64, _i64, _i64, _vp],
+    "mcv_w4a16_gemv_grouped": [_vp, _int, _i64, _vp],
     "mcv_gemv_f16": [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
     "mcv_lm_head_workspace_size": [_i64],
     "mcv_lm_head_argmax": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _sz, _vp],
@@ -128,9 +129,9 @@ def set_pdl(enabled: bool) -> None:
 class W4A16QuantizedWeight:
     """Device weight in the mcv-int4 layout (counterpart of the reference's
     W4A16QuantizedWeight, src/csrc/include/minicpmv/quantized_weight.h:11-17)."""
-    qweight: object   # torch.int32 [N, K/8]
-    scales: object    # torch.float16 [N, K/group]
-    zeros: object     # torch.int32 [N, ceil(G/8)]
+    qweight: object   # torch.int32 [Npad*K/8]  (Npad = N rounded up to 16)
+    scales: object    # torch.float16 [Npad, Gpad]  (Gpad = G rounded up to 8)
+    zeros: object     # torch.int32 [Npad, ceil(G/8)]
     zero_bias: int
     K: int
     N: int
@@ -143,9 +144,11 @@ class W4A16QuantizedWeight:
 
 def _alloc_layout_host(K: int, N: int, group: int):
     G = K // group
-    qw = np.empty((N, K // 8), np.uint32)
-    sc = np.empty((N, G), np.uint16)
-    zw = np.empty((N, (G + 7) // 8), np.uint32)
+    Np = (N + 15) // 16 * 16
+    Gp = (G + 7) // 8 * 8
+    qw = np.empty(Np * K // 8, np.uint32)
+    sc = np.empty((Np, Gp), np.uint16)
+    zw = np.empty((Np, (G + 7) // 8), np.uint32)
     return qw, sc, zw
 
 
@@ -217,6 +220,30 @@ def matmul_w4a16(x, w: W4A16QuantizedWeight, out, stream=None) -> None:
     M = x.shape[0] if x.dim() == 2 else 1
     _check(lib().mcv_w4a16_gemv(_ptr(x), _ptr(w.qweight), _ptr(w.scales), _ptr(w.zeros), w.zero_bias, _ptr(out),
                                 M, w.K, w.N, w.group_size, _stream(stream)), "matmul_w4a16")
+
+
+class W4A16Problem(ctypes.Structure):
+    """mirror of mcv_w4a16_problem (include/mcv_matmul.h)"""
+    _fields_ = [("x", _vp), ("qweight", _vp), ("scales", _vp), ("zeros", _vp), ("out", _vp),
+                ("K", ctypes.c_int32), ("N", ctypes.c_int32), ("group", ctypes.c_int32),
+                ("zero_bias", ctypes.c_int32)]
+
+
+def w4a16_problems(items):
+    """[(x, W4A16QuantizedWeight, out), ...] -> ctypes array for matmul_w4a16_grouped."""
+    arr = (W4A16Problem * len(items))()
+    for i, (x, w, out) in enumerate(items):
+        arr[i] = W4A16Problem(_ptr(x), _ptr(w.qweight), _ptr(w.scales), _ptr(w.zeros), _ptr(out),
+                              w.K, w.N, w.group_size, w.zero_bias)
+    return arr
+
+
+def matmul_w4a16_grouped(items, M: int = 1, stream=None, problems=None) -> None:
+    """Independent W4A16 GEMVs in one launch; items = [(x, weight, out), ...]
+    (or a prebuilt ``problems`` array from w4a16_problems)."""
+    arr = problems if problems is not None else w4a16_problems(items)
+    _check(lib().mcv_w4a16_gemv_grouped(ctypes.cast(arr, _vp), len(arr), M, _stream(stream)),
+           "matmul_w4a16_grouped")
 
 
 # ---- dense fp16 ----------------------------------------------------------------

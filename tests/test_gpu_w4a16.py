@@ -56,7 +56,7 @@ def test_config0_all_m(cuda, M):
 
 
 @pytest.mark.parametrize("K,N", [(1024, 16), (1024, 512), (1024, 6144), (2048, 1024), (3584, 1024),
-                                 (4096, 4096), (1024, 100), (128, 8), (8192, 64)])
+                                 (4096, 4096), (1024, 100), (128, 8), (8192, 64), (384, 40), (1152, 24)])
 def test_shapes(cuda, K, N):
     import mcv_b200
     x, q, z, s = synth.w4a16_inputs(1, K, N, seed=K * 7 + N)
@@ -127,3 +127,39 @@ def test_chained_gemvs_under_pdl(cuda):
         ref = oracle.w4a16_gemv(cur, oracle.w4a16_fold_zeros(q, z), s, nthreads=8)
         assert_f16_close(got, ref, what=f"chain step {i}")
         cur = got  # next step consumes exactly what the GPU produced
+
+
+@pytest.mark.parametrize("M", [1, 3, 8])
+def test_grouped_mixed_problems(cuda, M):
+    """One grouped launch over problems of different K/N (a linear-attention
+    layer's same-input projections plus unrelated ones), each checked alone."""
+    import mcv_b200
+    torch = cuda
+    shapes = [(1024, 6144), (1024, 2048), (1024, 16), (1024, 16), (2048, 1024), (3584, 1024), (1024, 100)]
+    items, refs = [], []
+    for i, (K, N) in enumerate(shapes):
+        x, q, z, s = synth.w4a16_inputs(M, K, N, seed=300 + i)
+        w = mcv_b200.pack_w4a16(q, z, s)
+        out = torch.empty((M, N), dtype=torch.float16, device="cuda")
+        items.append((torch.from_numpy(x).cuda(), w, out))
+        refs.append(oracle.w4a16_gemv(x, oracle.w4a16_fold_zeros(q, z), s, nthreads=8))
+    mcv_b200.matmul_w4a16_grouped(items, M=M)
+    torch.cuda.synchronize()
+    for (x, w, out), ref, (K, N) in zip(items, refs, shapes):
+        assert_f16_close(out.cpu().numpy(), ref, what=f"grouped K={K} N={N}")
+
+
+def test_grouped_more_than_one_launch(cuda):
+    import mcv_b200
+    torch = cuda
+    x, q, z, s = synth.w4a16_inputs(1, 1024, 512, seed=400)
+    w = mcv_b200.pack_w4a16(q, z, s)
+    xd = torch.from_numpy(x).cuda()
+    outs = [torch.empty((1, 512), dtype=torch.float16, device="cuda") for _ in range(100)]
+    mcv_b200.matmul_w4a16_grouped([(xd, w, o) for o in outs])
+    torch.cuda.synchronize()
+    ref = oracle.w4a16_gemv(x, oracle.w4a16_fold_zeros(q, z), s)
+    first = outs[0].cpu().numpy()
+    assert_f16_close(first, ref, what="grouped x100")
+    for o in outs[1:]:
+        assert np.array_equal(o.cpu().numpy().view(np.uint16), first.view(np.uint16))

@@ -22,21 +22,36 @@ def header_symbols():
     return sorted(set(re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\*?\s+\*?(mcv_[a-z0-9_]+)\(", text, re.M)))
 
 
+FRAG_SLOT = (0, 4, 1, 5, 2, 6, 3, 7)
+FRAG_ROW = (0, 0, 8, 8, 0, 0, 8, 8)
+FRAG_K = (0, 1, 0, 1, 8, 9, 8, 9)
+
+
 def decode_layout(w):
-    """mcv-int4 device arrays (numpy) -> (q-zero) int16 [K,N], scales [G,N]."""
+    """mcv-int4 device arrays (numpy) -> (q-zero) int16 [K,N], scales [G,N];
+    an independent decoder of the layout documented in include/mcv_matmul.h."""
     qw = w.qweight.cpu().numpy().view(np.uint32)
     sc = w.scales.cpu().numpy().view(np.uint16)
     zw = w.zeros.cpu().numpy().view(np.uint32)
-    N, kw = qw.shape
-    K = kw * 8
+    K, N = w.K, w.N
+    Np = (N + 15) // 16 * 16
     G = K // w.group_size
-    q = np.zeros((K, N), np.int16)
-    for i in range(8):
-        q[i::8, :] = ((qw >> np.uint32(4 * SLOT[i])) & np.uint32(0xF)).T.astype(np.int16)
-    z = np.zeros((G, N), np.int16)
-    for g in range(G):
-        z[g] = ((zw[:, g // 8] >> np.uint32(4 * (g % 8))) & np.uint32(0xF)).astype(np.int16) + w.zero_bias
-    return q - np.repeat(z, w.group_size, axis=0), sc.T
+    words = qw.reshape(Np // 16, K // 64, 32, 4)          # [strip, kq, lane, j]
+    words = words.transpose(0, 1, 3, 2).reshape(Np // 16, K // 16, 32)  # [strip, kb, lane]
+    q = np.zeros((K, Np), np.int16)
+    lane = np.arange(32)
+    g, t = lane // 4, lane % 4
+    for e in range(8):
+        vals = ((words >> np.uint32(4 * FRAG_SLOT[e])) & np.uint32(0xF)).astype(np.int16)
+        for strip in range(Np // 16):
+            n = strip * 16 + g + FRAG_ROW[e]
+            for kb in range(K // 16):
+                q[kb * 16 + 2 * t + FRAG_K[e], n] = vals[strip, kb]
+    z = np.zeros((G, Np), np.int16)
+    for gg in range(G):
+        z[gg] = ((zw[:, gg // 8] >> np.uint32(4 * (gg % 8))) & np.uint32(0xF)).astype(np.int16) + w.zero_bias
+    assert np.all(q[:, N:] == 0) and np.all(sc[N:] == 0) and np.all(sc[:, G:] == 0)
+    return (q - np.repeat(z, w.group_size, axis=0))[:, :N], sc[:N, :G].T
 
 
 def test_library_exports_every_header_symbol():
@@ -68,6 +83,8 @@ def test_status_strings_and_errors_without_device():
     assert st == 6
     st = L.mcv_w8a8_gemm_i32(fake, fake, fake, 1, 1000, 3584, 0, None)
     assert st == 2
+    st = L.mcv_w4a16_gemv(fake, fake, fake, fake, 0, fake, 1, 1024, 3584, 64, None)
+    assert st == 2 and b"128" in L.mcv_last_error()
     assert L.mcv_lm_head_workspace_size(1) >= 256 + 8 * 148 * 4
 
 
@@ -98,7 +115,7 @@ def host_pack(monkeypatch):
                             _FakeT(qw), _FakeT(sc), _FakeT(zw), int(zb), K, N, g))
 
 
-@pytest.mark.parametrize("K,N", [(1024, 3584), (3584, 1024), (256, 16)])
+@pytest.mark.parametrize("K,N", [(1024, 3584), (3584, 1024), (256, 16), (384, 40)])
 def test_pack_logical(host_pack, K, N):
     x, q, z, s = synth.w4a16_inputs(1, K, N, seed=K + N)
     w = mcv_b200.pack_w4a16(q, z, s)
