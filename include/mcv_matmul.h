@@ -57,6 +57,14 @@ int mcv_version(void);
 /* 1 (default): launch kernels with programmatic dependent launch; 0: plain launches. */
 void mcv_set_pdl(int enabled);
 
+/* Kernel-choice overrides for performance tuning; 0 restores the default.
+ *   MCV_TUNE_W4A16_MODE: 1 = persistent streaming kernel (each warp owns
+ *   whole 16-column strips), 2 = one block per strip with K split over its
+ *   warps (K <= 8192); default: K-split below 4 strips per SM. */
+enum mcv_tuning_key { MCV_TUNE_W4A16_MODE = 2, MCV_TUNE_COUNT = 8 };
+int mcv_set_tuning(int key, int value);
+int mcv_get_tuning(int key);
+
 /* ======================================================================== */
 /* W4A16: int4 weights, fp16 group scales and 4-bit zeros, fp16 activations */
 /* ======================================================================== */

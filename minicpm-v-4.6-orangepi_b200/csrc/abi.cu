@@ -10,6 +10,7 @@ namespace mcv {
 namespace {
 thread_local std::string g_last_error;
 std::atomic<int> g_pdl{1};
+std::atomic<int> g_tuning[MCV_TUNE_COUNT];
 }  // namespace
 
 void set_error(const std::string& msg) { g_last_error = msg; }
@@ -22,6 +23,10 @@ int fail(int status, const std::string& msg) {
 int cuda_fail(cudaError_t e, const char* what) {
     g_last_error = std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
     return MCV_ERR_CUDA;
+}
+
+int tuning(int key) {
+    return (key > 0 && key < MCV_TUNE_COUNT) ? g_tuning[key].load(std::memory_order_relaxed) : 0;
 }
 
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
@@ -64,5 +69,13 @@ const char* mcv_last_error(void) { return mcv::g_last_error.c_str(); }
 int mcv_version(void) { return (1 << 16) | 0; }
 
 void mcv_set_pdl(int enabled) { mcv::g_pdl.store(enabled ? 1 : 0); }
+
+int mcv_set_tuning(int key, int value) {
+    if (key <= 0 || key >= MCV_TUNE_COUNT) return mcv::fail(MCV_ERR_VALUE, "set_tuning: unknown key");
+    mcv::g_tuning[key].store(value);
+    return MCV_OK;
+}
+
+int mcv_get_tuning(int key) { return mcv::tuning(key); }
 
 }  // extern "C"

@@ -20,6 +20,7 @@ void set_error(const std::string& msg);
 int fail(int status, const std::string& msg);
 int cuda_fail(cudaError_t e, const char* what);
 bool pdl_enabled();
+int tuning(int key);
 
 #define MCV_CHECK_CUDA(expr)                                   \
     do {                                                       \

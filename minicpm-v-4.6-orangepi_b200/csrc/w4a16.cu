@@ -229,6 +229,102 @@ w4a16_gemv_kernel(const __grid_constant__ GroupParams gp) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// K-split variant for launches with few strips (a single decode GEMV): one
+// block per strip, its 8 warps take the strip's 128-k groups round-robin (at
+// most KG each), load all their weight vectors, scales and zeros before
+// griddepcontrol.wait, and meet in shared memory for the final sum.  This
+// keeps a lone GEMV's critical path to one load latency plus 1/8 of its math.
+// ---------------------------------------------------------------------------
+template <int M, int KG>
+__global__ void __launch_bounds__(kWarps * 32)
+w4a16_ksplit_kernel(const __grid_constant__ GroupParams gp) {
+    __shared__ float4 red[kWarps][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int strip = static_cast<int>(blockIdx.x);
+    const int pi = find_problem(gp, strip, 0);
+    const Problem& P = gp.p[pi];
+    const int K = P.K, G = K / kGroup, Gp = (G + 7) & ~7, zw = (G + 7) >> 3;
+    const int sl = strip - P.strip_begin;
+    const int col = sl * 16 + g;
+    uint4 v[KG][2];
+    float slo[KG], shi[KG];
+    int zlo[KG], zhi[KG];
+#pragma unroll
+    for (int j = 0; j < KG; ++j) {
+        const int gi = warp + j * kWarps;
+        v[j][0] = v[j][1] = make_uint4(0, 0, 0, 0);
+        slo[j] = shi[j] = 0.0f;
+        zlo[j] = zhi[j] = 0;
+        if (gi < G) {
+            const size_t base = (static_cast<size_t>(sl) * (K / 64) + 2 * gi) * 32 + lane;
+            v[j][0] = ld_stream(P.qw + base);
+            v[j][1] = ld_stream(P.qw + base + 32);
+            slo[j] = __half2float(P.s[static_cast<size_t>(col) * Gp + gi]);
+            shi[j] = __half2float(P.s[static_cast<size_t>(col + 8) * Gp + gi]);
+            zlo[j] = static_cast<int>((P.z[static_cast<size_t>(col) * zw + (gi >> 3)] >> (4 * (gi & 7))) & 0xfu);
+            zhi[j] = static_cast<int>((P.z[static_cast<size_t>(col + 8) * zw + (gi >> 3)] >> (4 * (gi & 7))) & 0xfu);
+        }
+    }
+    pdl_trigger();
+    pdl_wait();  // x may be the previous kernel's output
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const __half2 inv16 = __halves2half2(__ushort_as_half(0x2c00), __ushort_as_half(0x2c00));
+#pragma unroll
+    for (int j = 0; j < KG; ++j) {
+        const int gi = warp + j * kWarps;
+        if (gi >= G) break;
+        uint32_t bx[8][2];
+        const __half* xrow = P.x + static_cast<size_t>(g) * K + gi * kGroup + 2 * t;
+#pragma unroll
+        for (int kb = 0; kb < 8; ++kb) {
+            bx[kb][0] = bx[kb][1] = 0u;
+            if (g < M) {
+                bx[kb][0] = *reinterpret_cast<const uint32_t*>(xrow + kb * 16);
+                bx[kb][1] = *reinterpret_cast<const uint32_t*>(xrow + kb * 16 + 8);
+            }
+        }
+        const __half z1 = __int2half_rn(1024 + zlo[j] + P.zero_bias);
+        const __half z2 = __int2half_rn(-(64 + zhi[j] + P.zero_bias));
+        const __half2 zl = __halves2half2(z1, z1), zh = __halves2half2(z2, z2);
+        float e[4] = {0.0f, 0.0f, 0.0f, 0.0f}, o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int kb = 0; kb < 8; ++kb) {
+            const uint4 vv = v[j][kb >> 2];
+            const uint32_t w = (kb & 3) == 0 ? vv.x : (kb & 3) == 1 ? vv.y : (kb & 3) == 2 ? vv.z : vv.w;
+            const uint32_t w8 = w >> 8;
+            constexpr uint32_t kMagic = 0x64006400u;
+            uint32_t a[4];
+            a[0] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w, 0x000f000fu, kMagic)), zl));
+            a[1] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w, 0x00f000f0u, kMagic)), inv16, zh));
+            a[2] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w8, 0x000f000fu, kMagic)), zl));
+            a[3] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w8, 0x00f000f0u, kMagic)), inv16, zh));
+            if (kb & 1) mma_16816(o, a, bx[kb][0], bx[kb][1]);
+            else mma_16816(e, a, bx[kb][0], bx[kb][1]);
+        }
+        acc[0] = fmaf(e[0] + o[0], slo[j], acc[0]);
+        acc[1] = fmaf(e[1] + o[1], slo[j], acc[1]);
+        acc[2] = fmaf(e[2] + o[2], shi[j], acc[2]);
+        acc[3] = fmaf(e[3] + o[3], shi[j], acc[3]);
+    }
+    red[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    __syncthreads();
+    if (warp == 0) {
+        float4 sum = red[0][lane];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) {
+            const float4 r = red[w][lane];
+            sum.x += r.x;
+            sum.y += r.y;
+            sum.z += r.z;
+            sum.w += r.w;
+        }
+        const float out4[4] = {sum.x, sum.y, sum.z, sum.w};
+        store_strip<M>(P, sl, lane, out4);
+    }
+}
+
 int assign_strips(GroupParams& gp) {
     int t = 0;
     for (int i = 0; i < gp.count; ++i) {
@@ -242,6 +338,20 @@ int assign_strips(GroupParams& gp) {
 template <int M>
 int launch_m(GroupParams& gp, cudaStream_t st) {
     const int strips = assign_strips(gp);
+    const int mode = tuning(MCV_TUNE_W4A16_MODE);
+    // few strips: one block per strip with K split over its warps; many
+    // strips: the persistent streaming kernel
+    if (mode == 2 || (mode == 0 && strips < sm_count() * 4)) {
+        int maxG = 0;
+        for (int i = 0; i < gp.count; ++i) maxG = std::max(maxG, gp.p[i].K / kGroup);
+        const int per_warp = (maxG + kWarps - 1) / kWarps;
+        auto go = [&](auto kern) { return launch(kern, dim3(strips), dim3(kWarps * 32), 0, st, gp); };
+        if (per_warp <= 1) return go(w4a16_ksplit_kernel<M, 1>);
+        if (per_warp <= 2) return go(w4a16_ksplit_kernel<M, 2>);
+        if (per_warp <= 4) return go(w4a16_ksplit_kernel<M, 4>);
+        if (per_warp <= 8) return go(w4a16_ksplit_kernel<M, 8>);
+        // larger K: the streaming kernel has no K limit
+    }
     // spread strips over SMs first; at most kBlocksPerSm resident blocks per SM
     const int blocks = std::min(strips, sm_count() * kBlocksPerSm);
     return launch(w4a16_gemv_kernel<M>, dim3(blocks), dim3(kWarps * 32), 0, st, gp);

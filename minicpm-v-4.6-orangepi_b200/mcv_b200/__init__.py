@@ -36,6 +36,8 @@ _SIGS = {
     "mcv_last_error": [],
     "mcv_version": [],
     "mcv_set_pdl": [_int],
+    "mcv_set_tuning": [_int, _int],
+    "mcv_get_tuning": [_int],
     "mcv_w4a16_layout_bytes": [_i64, _i64, _i64, _vp, _vp, _vp],
     "mcv_w4a16_pack_host": [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp],
     "mcv_w4a16_pack_gptq_host": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp],
@@ -121,6 +123,13 @@ def _ptr(t):
 
 def set_pdl(enabled: bool) -> None:
     lib().mcv_set_pdl(1 if enabled else 0)
+
+
+TUNE_W4A16_MODE = 2
+
+
+def set_tuning(key: int, value: int) -> None:
+    _check(lib().mcv_set_tuning(key, value), "set_tuning")
 
 
 # ---- W4A16 ------------------------------------------------------------------

@@ -163,3 +163,19 @@ def test_grouped_more_than_one_launch(cuda):
     assert_f16_close(first, ref, what="grouped x100")
     for o in outs[1:]:
         assert np.array_equal(o.cpu().numpy().view(np.uint16), first.view(np.uint16))
+
+
+@pytest.mark.parametrize("mode", [1, 2])
+@pytest.mark.parametrize("M,K,N", [(1, 1024, 3584), (3, 3584, 1024), (8, 384, 200), (2, 8192, 64)])
+def test_both_kernels_agree(cuda, mode, M, K, N):
+    """The streaming kernel (mode 1) and the K-split kernel (mode 2)."""
+    import mcv_b200
+    x, q, z, s = synth.w4a16_inputs(M, K, N, seed=K + N + M)
+    w = mcv_b200.pack_w4a16(q, z, s)
+    ref = oracle.w4a16_gemv(x, oracle.w4a16_fold_zeros(q, z), s, nthreads=8)
+    mcv_b200.set_tuning(mcv_b200.TUNE_W4A16_MODE, mode)
+    try:
+        out = run_gemv(cuda, x, w)
+    finally:
+        mcv_b200.set_tuning(mcv_b200.TUNE_W4A16_MODE, 0)
+    assert_f16_close(out, ref, what=f"mode={mode}")
