@@ -72,13 +72,15 @@ int mcv_get_tuning(int key);
  * Device weight layout "mcv-int4" (prepared once at load time; group = 128,
  * the only quantization group the reference supports, ops.h:95-103):
  *   qweight  uint32 [Npad/16][K/64][32][4]   Npad = N rounded up to 16.
- *            Output columns form strips of 16; per strip, groups of four
- *            16-k blocks follow each other; entry [s][kq][l][j] is lane l's
- *            word for k-block 4*kq+j: the eight 4-bit values lane l feeds to
- *            one m16n8k16 tensor-core MMA as its A fragment (rows = the
- *            strip's columns), (col, k) = (l/4, 2(l%4)), (l/4, 2(l%4)+1),
- *            (l/4+8, 2(l%4)), (l/4+8, 2(l%4)+1), then the same at k+8, in
- *            nibble slots 0,4,1,5,2,6,3,7.
+ *            Output columns form strips of 16; per strip, 64-k quads follow
+ *            each other; entry [s][q][l][j] is lane l's word for the j-th
+ *            MMA of quad q: the eight 4-bit values it feeds to one m16n8k16
+ *            tensor-core MMA as its A fragment (rows = the strip's columns).
+ *            With kb = 64q + 16(l%4) + 4j, they are (col, k) = (l/4, kb),
+ *            (l/4, kb+1), (l/4+8, kb), (l/4+8, kb+1), (l/4, kb+2),
+ *            (l/4, kb+3), (l/4+8, kb+2), (l/4+8, kb+3), in nibble slots
+ *            0,4,1,5,2,6,3,7 (k is permuted inside each quad identically for
+ *            weights and activations, which leaves every dot product intact).
  *   scales   fp16   [Npad][Gpad]   G = K/128, Gpad = G rounded up to 8
  *   zeros    uint32 [Npad][ceil(G/8)]  4-bit zero of (g, n) at nibble g%8 of
  *            word g/8; effective zero = nibble + zero_bias
@@ -128,8 +130,8 @@ int mcv_w4a16_pack_from_tiles_host(const int8_t* packed, int64_t tile_len,
                                    uint32_t* zeros_out, int* zero_bias_out);
 
 /* out[m][n] = sum_k x[m][k] * w[k][n], M = 1..8, fp32 accumulation, fp16 out.
- * x fp16 [M][K] (4-byte aligned), out fp16 [M][N]; group must be 128;
- * qweight and scales 16-byte aligned.
+ * x fp16 [M][K], out fp16 [M][N]; group must be 128; x, qweight and scales
+ * 16-byte aligned.
  * Replaces matmul_w4a16 (src/csrc/lib/ops.cpp:1030-1095, ops.h:95-108; M=1
  * there) and its kernel op_kernel/matmul_w4a16_custom.cpp. */
 int mcv_w4a16_gemv(const void* x, const void* qweight, const void* scales, const void* zeros,

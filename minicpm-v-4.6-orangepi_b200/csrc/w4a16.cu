@@ -47,13 +47,69 @@ constexpr int kMaxGroupProblems = 48;
 inline int64_t padded_n(int64_t N) { return (N + 15) / 16 * 16; }
 inline int64_t padded_g(int64_t G) { return (G + 7) / 8 * 8; }
 
-// Fragment element e of lane (g = lane/4, t = lane%4):
-// (row, k) = (g, 2t), (g, 2t+1), (g+8, 2t), (g+8, 2t+1), then the same at k+8.
-// Nibble slots are chosen so that LOP3 with 0x000F000F / 0x00F000F0 on the
-// word and on word >> 8 yields the four half2 registers a0..a3 in order.
+// An MMA's dot product does not depend on the order of k, so k is permuted
+// inside every 64-k quad, identically for weights and activations: lane
+// (g = lane/4, t = lane%4) owns physical k = 16t .. 16t+15 of the quad, and
+// k-block j of the quad uses its k = 16t + 4j .. 16t + 4j + 3.  Fragment
+// element e of the lane's A word for k-block j is then
+// (row, k) = (g, +0), (g, +1), (g+8, +0), (g+8, +1), (g, +2), (g, +3),
+// (g+8, +2), (g+8, +3) relative to 16t + 4j, and the B fragment is x at the
+// same four k - one 16-byte load of x covers two k-blocks.  Nibble slots are
+// chosen so that LOP3 with 0x000F000F / 0x00F000F0 on the word and on
+// word >> 8 yields the four half2 registers a0..a3 in order.
 constexpr int kFragSlot[8] = {0, 4, 1, 5, 2, 6, 3, 7};
 constexpr int kFragRow[8] = {0, 0, 8, 8, 0, 0, 8, 8};
-constexpr int kFragK[8] = {0, 1, 0, 1, 8, 9, 8, 9};
+constexpr int kFragK[8] = {0, 1, 0, 1, 2, 3, 2, 3};
+
+__device__ __forceinline__ void mma_16816(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// One 128-k group for one lane: v[0], v[1] are the lane's weight vectors of
+// the group's two quads, xg points at x[row g][group start + 16t] (read only
+// when g < M).  Dequantises and runs 8 MMAs on four independent accumulator
+// chains; returns the group's fp32 sums for rows g, g+8 x columns 2t, 2t+1.
+template <int M>
+__device__ __forceinline__ void group_mma(const uint4 (&v)[2], const __half* xg, int g, int zl_q, int zh_q,
+                                          float d[4]) {
+    uint4 xv[2][2];
+#pragma unroll
+    for (int qd = 0; qd < 2; ++qd) {
+        xv[qd][0] = xv[qd][1] = make_uint4(0, 0, 0, 0);
+        if (g < M) {
+            xv[qd][0] = *reinterpret_cast<const uint4*>(xg + qd * 64);
+            xv[qd][1] = *reinterpret_cast<const uint4*>(xg + qd * 64 + 8);
+        }
+    }
+    const __half z1 = __int2half_rn(1024 + zl_q);   // rows g: 1024 + zero
+    const __half z2 = __int2half_rn(-(64 + zh_q));  // rows g+8: -(64 + zero)
+    const __half2 zl = __halves2half2(z1, z1), zh = __halves2half2(z2, z2);
+    const __half2 inv16 = __halves2half2(__ushort_as_half(0x2c00), __ushort_as_half(0x2c00));
+    float c[4][4] = {};
+#pragma unroll
+    for (int kb = 0; kb < 8; ++kb) {
+        const int qd = kb >> 2, j = kb & 3;
+        const uint4 vv = v[qd];
+        const uint32_t w = j == 0 ? vv.x : j == 1 ? vv.y : j == 2 ? vv.z : vv.w;
+        const uint4 xx = xv[qd][j >> 1];
+        const uint32_t b0 = (j & 1) ? xx.z : xx.x;
+        const uint32_t b1 = (j & 1) ? xx.w : xx.y;
+        const uint32_t w8 = w >> 8;
+        constexpr uint32_t kMagic = 0x64006400u;
+        uint32_t a[4];
+        a[0] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w, 0x000f000fu, kMagic)), zl));
+        a[1] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w, 0x00f000f0u, kMagic)), inv16, zh));
+        a[2] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w8, 0x000f000fu, kMagic)), zl));
+        a[3] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w8, 0x00f000f0u, kMagic)), inv16, zh));
+        mma_16816(c[kb & 3], a, b0, b1);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] = (c[0][i] + c[1][i]) + (c[2][i] + c[3][i]);
+}
 
 struct Problem {
     const __half* x;
@@ -71,13 +127,6 @@ struct GroupParams {
     Problem p[kMaxGroupProblems];
 };
 
-__device__ __forceinline__ void mma_16816(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
 
 __device__ __forceinline__ int find_problem(const GroupParams& gp, int strip, int start) {
     int pi = start;
@@ -120,47 +169,19 @@ __device__ __forceinline__ void compute_chunk(const Chunk& b, const Problem& P, 
     const int K = P.K;
     const int nq = min(8, (K - c * kChunkK) / 64);
     const int g = lane >> 2, t = lane & 3;
-    const __half* xrow = P.x + static_cast<size_t>(g) * K + c * kChunkK + 2 * t;
-    const __half2 inv16 = __halves2half2(__ushort_as_half(0x2c00), __ushort_as_half(0x2c00));
+    const __half* xrow = P.x + static_cast<size_t>(g) * K + c * kChunkK + 16 * t;
 #pragma unroll
     for (int gi = 0; gi < 4; ++gi) {
         if (2 * gi >= nq) break;
-        uint32_t bx[8][2];
-#pragma unroll
-        for (int kb = 0; kb < 8; ++kb) {
-            bx[kb][0] = bx[kb][1] = 0u;
-            if (g < M) {
-                const __half* p = xrow + gi * kGroup + kb * 16;
-                bx[kb][0] = *reinterpret_cast<const uint32_t*>(p);
-                bx[kb][1] = *reinterpret_cast<const uint32_t*>(p + 8);
-            }
-        }
-        const int zl_q = static_cast<int>((b.zlo >> (4 * gi)) & 0xfu) + P.zero_bias;
-        const int zh_q = static_cast<int>((b.zhi >> (4 * gi)) & 0xfu) + P.zero_bias;
-        const __half z1 = __int2half_rn(1024 + zl_q);   // rows g: 1024 + zero
-        const __half z2 = __int2half_rn(-(64 + zh_q));  // rows g+8: -(64 + zero)
-        const __half2 zl = __halves2half2(z1, z1);
-        const __half2 zh = __halves2half2(z2, z2);
-        float e[4] = {0.0f, 0.0f, 0.0f, 0.0f}, o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-        for (int kb = 0; kb < 8; ++kb) {
-            const uint4 v = b.w[2 * gi + (kb >> 2)];
-            const uint32_t w = (kb & 3) == 0 ? v.x : (kb & 3) == 1 ? v.y : (kb & 3) == 2 ? v.z : v.w;
-            const uint32_t w8 = w >> 8;
-            constexpr uint32_t kMagic = 0x64006400u;
-            uint32_t a[4];
-            a[0] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w, 0x000f000fu, kMagic)), zl));
-            a[1] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w, 0x00f000f0u, kMagic)), inv16, zh));
-            a[2] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w8, 0x000f000fu, kMagic)), zl));
-            a[3] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w8, 0x00f000f0u, kMagic)), inv16, zh));
-            if (kb & 1) mma_16816(o, a, bx[kb][0], bx[kb][1]);
-            else mma_16816(e, a, bx[kb][0], bx[kb][1]);
-        }
+        const uint4 v[2] = {b.w[2 * gi], b.w[2 * gi + 1]};
+        float d[4];
+        group_mma<M>(v, xrow + gi * kGroup, g, static_cast<int>((b.zlo >> (4 * gi)) & 0xfu) + P.zero_bias,
+                     static_cast<int>((b.zhi >> (4 * gi)) & 0xfu) + P.zero_bias, d);
         const float s_lo = half_of(b.slo, gi), s_hi = half_of(b.shi, gi);
-        acc[0] = fmaf(e[0] + o[0], s_lo, acc[0]);
-        acc[1] = fmaf(e[1] + o[1], s_lo, acc[1]);
-        acc[2] = fmaf(e[2] + o[2], s_hi, acc[2]);
-        acc[3] = fmaf(e[3] + o[3], s_hi, acc[3]);
+        acc[0] = fmaf(d[0], s_lo, acc[0]);
+        acc[1] = fmaf(d[1], s_lo, acc[1]);
+        acc[2] = fmaf(d[2], s_hi, acc[2]);
+        acc[3] = fmaf(d[3], s_hi, acc[3]);
     }
 }
 
@@ -270,43 +291,17 @@ w4a16_ksplit_kernel(const __grid_constant__ GroupParams gp) {
     pdl_trigger();
     pdl_wait();  // x may be the previous kernel's output
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    const __half2 inv16 = __halves2half2(__ushort_as_half(0x2c00), __ushort_as_half(0x2c00));
 #pragma unroll
     for (int j = 0; j < KG; ++j) {
         const int gi = warp + j * kWarps;
         if (gi >= G) break;
-        uint32_t bx[8][2];
-        const __half* xrow = P.x + static_cast<size_t>(g) * K + gi * kGroup + 2 * t;
-#pragma unroll
-        for (int kb = 0; kb < 8; ++kb) {
-            bx[kb][0] = bx[kb][1] = 0u;
-            if (g < M) {
-                bx[kb][0] = *reinterpret_cast<const uint32_t*>(xrow + kb * 16);
-                bx[kb][1] = *reinterpret_cast<const uint32_t*>(xrow + kb * 16 + 8);
-            }
-        }
-        const __half z1 = __int2half_rn(1024 + zlo[j] + P.zero_bias);
-        const __half z2 = __int2half_rn(-(64 + zhi[j] + P.zero_bias));
-        const __half2 zl = __halves2half2(z1, z1), zh = __halves2half2(z2, z2);
-        float e[4] = {0.0f, 0.0f, 0.0f, 0.0f}, o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-        for (int kb = 0; kb < 8; ++kb) {
-            const uint4 vv = v[j][kb >> 2];
-            const uint32_t w = (kb & 3) == 0 ? vv.x : (kb & 3) == 1 ? vv.y : (kb & 3) == 2 ? vv.z : vv.w;
-            const uint32_t w8 = w >> 8;
-            constexpr uint32_t kMagic = 0x64006400u;
-            uint32_t a[4];
-            a[0] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w, 0x000f000fu, kMagic)), zl));
-            a[1] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w, 0x00f000f0u, kMagic)), inv16, zh));
-            a[2] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w8, 0x000f000fu, kMagic)), zl));
-            a[3] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w8, 0x00f000f0u, kMagic)), inv16, zh));
-            if (kb & 1) mma_16816(o, a, bx[kb][0], bx[kb][1]);
-            else mma_16816(e, a, bx[kb][0], bx[kb][1]);
-        }
-        acc[0] = fmaf(e[0] + o[0], slo[j], acc[0]);
-        acc[1] = fmaf(e[1] + o[1], slo[j], acc[1]);
-        acc[2] = fmaf(e[2] + o[2], shi[j], acc[2]);
-        acc[3] = fmaf(e[3] + o[3], shi[j], acc[3]);
+        float d[4];
+        group_mma<M>(v[j], P.x + static_cast<size_t>(g) * K + gi * kGroup + 16 * t, g, zlo[j] + P.zero_bias,
+                     zhi[j] + P.zero_bias, d);
+        acc[0] = fmaf(d[0], slo[j], acc[0]);
+        acc[1] = fmaf(d[1], slo[j], acc[1]);
+        acc[2] = fmaf(d[2], shi[j], acc[2]);
+        acc[3] = fmaf(d[3], shi[j], acc[3]);
     }
     red[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
     __syncthreads();
@@ -389,12 +384,11 @@ void pack_layout(QF q, ZF z, const uint16_t* scales_gn, int64_t K, int64_t N, in
         for (int64_t kq = 0; kq < KQ; ++kq)
             for (int lane = 0; lane < 32; ++lane)
                 for (int j = 0; j < 4; ++j) {  // k-block 4*kq + j -> component j of the lane vector
-                    const int64_t kb = kq * 4 + j;
                     const int gg = lane >> 2, t = lane & 3;
                     uint32_t word = 0;
                     for (int e = 0; e < 8; ++e) {
                         const int64_t n = strip * 16 + gg + kFragRow[e];
-                        const int64_t k = kb * 16 + 2 * t + kFragK[e];
+                        const int64_t k = kq * 64 + 16 * t + 4 * j + kFragK[e];
                         const uint32_t v = n < N ? (static_cast<uint32_t>(q(k, n)) & 0xfu) : 0u;
                         word |= v << (4 * kFragSlot[e]);
                     }
@@ -550,10 +544,10 @@ int mcv_w4a16_gemv_grouped(const mcv_w4a16_problem* problems, int count, int64_t
         if (!p.x || !p.qweight || !p.scales || !p.zeros || !p.out) return fail(MCV_ERR_NULL, "w4a16_gemv: null pointer");
         int st = check_layout_dims(p.K, p.N, p.group);
         if (st) return st;
-        if (!aligned16(p.qweight) || !aligned16(p.scales))
-            return fail(MCV_ERR_ALIGN, "w4a16_gemv: qweight and scales must be 16-byte aligned");
-        if ((reinterpret_cast<uintptr_t>(p.x) | reinterpret_cast<uintptr_t>(p.zeros)) & 3u)
-            return fail(MCV_ERR_ALIGN, "w4a16_gemv: x and zeros must be 4-byte aligned");
+        if (!aligned16(p.qweight) || !aligned16(p.scales) || !aligned16(p.x))
+            return fail(MCV_ERR_ALIGN, "w4a16_gemv: x, qweight and scales must be 16-byte aligned");
+        if (reinterpret_cast<uintptr_t>(p.zeros) & 3u)
+            return fail(MCV_ERR_ALIGN, "w4a16_gemv: zeros must be 4-byte aligned");
         if (p.zero_bias < 0 || p.zero_bias > 1) return fail(MCV_ERR_VALUE, "w4a16_gemv: zero_bias must be 0 or 1");
     }
     auto st = static_cast<cudaStream_t>(stream);

@@ -24,7 +24,7 @@ def header_symbols():
 
 FRAG_SLOT = (0, 4, 1, 5, 2, 6, 3, 7)
 FRAG_ROW = (0, 0, 8, 8, 0, 0, 8, 8)
-FRAG_K = (0, 1, 0, 1, 8, 9, 8, 9)
+FRAG_K = (0, 1, 0, 1, 2, 3, 2, 3)
 
 
 def decode_layout(w):
@@ -36,17 +36,16 @@ def decode_layout(w):
     K, N = w.K, w.N
     Np = (N + 15) // 16 * 16
     G = K // w.group_size
-    words = qw.reshape(Np // 16, K // 64, 32, 4)          # [strip, kq, lane, j]
-    words = words.transpose(0, 1, 3, 2).reshape(Np // 16, K // 16, 32)  # [strip, kb, lane]
+    words = qw.reshape(Np // 16, K // 64, 32, 4)          # [strip, quad, lane, j]
     q = np.zeros((K, Np), np.int16)
-    lane = np.arange(32)
-    g, t = lane // 4, lane % 4
-    for e in range(8):
-        vals = ((words >> np.uint32(4 * FRAG_SLOT[e])) & np.uint32(0xF)).astype(np.int16)
-        for strip in range(Np // 16):
-            n = strip * 16 + g + FRAG_ROW[e]
-            for kb in range(K // 16):
-                q[kb * 16 + 2 * t + FRAG_K[e], n] = vals[strip, kb]
+    for lane in range(32):
+        g, t = lane // 4, lane % 4
+        for j in range(4):
+            for e in range(8):
+                vals = ((words[:, :, lane, j] >> np.uint32(4 * FRAG_SLOT[e])) & np.uint32(0xF)).astype(np.int16)
+                n = np.arange(Np // 16) * 16 + g + FRAG_ROW[e]          # [strip]
+                k = np.arange(K // 64) * 64 + 16 * t + 4 * j + FRAG_K[e]  # [quad]
+                q[np.ix_(k, n)] = vals.T
     z = np.zeros((G, Np), np.int16)
     for gg in range(G):
         z[gg] = ((zw[:, gg // 8] >> np.uint32(4 * (gg % 8))) & np.uint32(0xF)).astype(np.int16) + w.zero_bias
