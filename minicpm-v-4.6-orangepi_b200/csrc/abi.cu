@@ -7,6 +7,8 @@
 
 namespace mcv {
 
+unsigned take_w4a16_device_error();
+
 namespace {
 thread_local std::string g_last_error;
 std::atomic<int> g_pdl{1};
@@ -77,5 +79,10 @@ int mcv_set_tuning(int key, int value) {
 }
 
 int mcv_get_tuning(int key) { return mcv::tuning(key); }
+
+unsigned mcv_device_errors(void) {
+    cudaDeviceSynchronize();
+    return mcv::take_w4a16_device_error();
+}
 
 }  // extern "C"

@@ -251,6 +251,126 @@ w4a16_gemv_kernel(const __grid_constant__ GroupParams gp) {
 }
 
 // ---------------------------------------------------------------------------
+// Streaming variant with warp-private bulk-copy rings.  Each warp owns whole
+// strips as above, but its (strip, 512-k chunk) items arrive in shared
+// memory: lane 0 moves the chunk's weights (one contiguous <= 4 KB range)
+// with cp.async.bulk, lanes copy the chunk's scales (8 bytes per column) and
+// zero words with cp.async, and the stage's mbarrier completes when all of it
+// has landed.  Each warp keeps kRing items in flight (128 KB per SM) without
+// spending registers on them, and needs no synchronisation with other warps.
+// The first kRing items are requested before griddepcontrol.wait.
+// ---------------------------------------------------------------------------
+constexpr int kRing = 4;
+constexpr int kStageW = 4096;                      // 8 lane vectors x 32 lanes
+constexpr int kStageBytes = kStageW + 16 * 8 + 16 * 4 + 64;  // + scales + zeros, 4352
+constexpr int kTmaSmem = kWarps * kRing * kStageBytes + kWarps * kRing * 8;
+
+static __device__ unsigned g_w4a16_dev_error;
+
+struct ItemIter {
+    int strip, c, pi;
+};
+
+__device__ __forceinline__ void next_item(const GroupParams& gp, ItemIter& it, int W) {
+    const int nchunks = (gp.p[it.pi].K + kChunkK - 1) / kChunkK;
+    if (++it.c == nchunks) {
+        it.c = 0;
+        it.strip += W;
+        if (it.strip < gp.total_strips) it.pi = find_problem(gp, it.strip, it.pi);
+    }
+}
+
+// Requests item `it` into stage `st` (whole warp participates).
+__device__ __forceinline__ void issue_item(const GroupParams& gp, const ItemIter& it, unsigned char* st,
+                                           uint64_t* bar, int lane) {
+    const Problem& P = gp.p[it.pi];
+    const int K = P.K, G = K / kGroup, Gp = (G + 7) & ~7, zw = (G + 7) >> 3;
+    const int sl = it.strip - P.strip_begin;
+    const int nq = min(8, (K - it.c * kChunkK) / 64);
+    if (lane == 0) {
+        const uint32_t bytes = static_cast<uint32_t>(nq) * 32u * 16u;
+        mbar_expect_tx(bar, bytes);
+        bulk_load(st, P.qw + (static_cast<size_t>(sl) * (K / 64) + it.c * 8) * 32, bytes, bar);
+    }
+    const int col = sl * 16 + (lane & 15);
+    if (lane < 16) cp_async8(st + kStageW + lane * 8, P.s + static_cast<size_t>(col) * Gp + it.c * 4);
+    else cp_async4(st + kStageW + 128 + (lane - 16) * 4, P.z + static_cast<size_t>(col) * zw + (it.c >> 1));
+    cp_async_mbar_arrive(bar);
+}
+
+template <int M>
+__global__ void __launch_bounds__(kWarps * 32, 1)
+w4a16_tma_kernel(const __grid_constant__ GroupParams gp) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    unsigned char* ring = smem + warp * kRing * kStageBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * kRing * kStageBytes) + warp * kRing;
+    const int W = static_cast<int>(gridDim.x) * kWarps;
+    const int T = gp.total_strips;
+    ItemIter cur{warp * static_cast<int>(gridDim.x) + static_cast<int>(blockIdx.x), 0, 0};
+    if (cur.strip < T) cur.pi = find_problem(gp, cur.strip, 0);
+    if (lane == 0)
+        for (int s = 0; s < kRing; ++s) mbar_init(&bars[s], 1 + 32);  // bulk arrival + 32 cp.async lanes
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    __syncwarp();
+    ItemIter iss = cur;
+    int issued = 0;
+    for (; issued < kRing && iss.strip < T; ++issued) {
+        issue_item(gp, iss, ring + issued * kStageBytes, &bars[issued], lane);
+        next_item(gp, iss, W);
+    }
+    pdl_trigger();
+    pdl_wait();  // x may be the previous kernel's output
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 1
+    for (int k = 0; cur.strip < T; ++k) {
+        const int s = k % kRing;
+        if (!mbar_wait(&bars[s], static_cast<uint32_t>(k / kRing) & 1u)) {
+            if (lane == 0) atomicOr(&g_w4a16_dev_error, kDevErrTimeout);
+            return;
+        }
+        const Problem& P = gp.p[cur.pi];
+        const int K = P.K;
+        const int nq = min(8, (K - cur.c * kChunkK) / 64);
+        const unsigned char* st = ring + s * kStageBytes;
+        const uint2 slo = *reinterpret_cast<const uint2*>(st + kStageW + g * 8);
+        const uint2 shi = *reinterpret_cast<const uint2*>(st + kStageW + (g + 8) * 8);
+        const int sh = 16 * (cur.c & 1);
+        const uint32_t zlo = *reinterpret_cast<const uint32_t*>(st + kStageW + 128 + g * 4) >> sh;
+        const uint32_t zhi = *reinterpret_cast<const uint32_t*>(st + kStageW + 128 + (g + 8) * 4) >> sh;
+        const __half* xrow = P.x + static_cast<size_t>(g) * K + cur.c * kChunkK + 16 * t;
+#pragma unroll
+        for (int gi = 0; gi < 4; ++gi) {
+            if (2 * gi >= nq) break;
+            const uint4 v[2] = {*reinterpret_cast<const uint4*>(st + (2 * gi * 32 + lane) * 16),
+                                *reinterpret_cast<const uint4*>(st + ((2 * gi + 1) * 32 + lane) * 16)};
+            float d[4];
+            group_mma<M>(v, xrow + gi * kGroup, g, static_cast<int>((zlo >> (4 * gi)) & 0xfu) + P.zero_bias,
+                         static_cast<int>((zhi >> (4 * gi)) & 0xfu) + P.zero_bias, d);
+            const float s_lo = half_of(slo, gi), s_hi = half_of(shi, gi);
+            acc[0] = fmaf(d[0], s_lo, acc[0]);
+            acc[1] = fmaf(d[1], s_lo, acc[1]);
+            acc[2] = fmaf(d[2], s_hi, acc[2]);
+            acc[3] = fmaf(d[3], s_hi, acc[3]);
+        }
+        const int nchunks = (K + kChunkK - 1) / kChunkK;
+        if (cur.c + 1 == nchunks) {
+            store_strip<M>(P, cur.strip - P.strip_begin, lane, acc);
+            acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
+        }
+        // refill this stage with the item kRing ahead
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (iss.strip < T) {
+            issue_item(gp, iss, ring + s * kStageBytes, &bars[s], lane);
+            next_item(gp, iss, W);
+        }
+        next_item(gp, cur, W);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // K-split variant for launches with few strips (a single decode GEMV): one
 // block per strip, its 8 warps take the strip's 128-k groups round-robin (at
 // most KG each), load all their weight vectors, scales and zeros before
@@ -347,9 +467,16 @@ int launch_m(GroupParams& gp, cudaStream_t st) {
         if (per_warp <= 8) return go(w4a16_ksplit_kernel<M, 8>);
         // larger K: the streaming kernel has no K limit
     }
-    // spread strips over SMs first; at most kBlocksPerSm resident blocks per SM
-    const int blocks = std::min(strips, sm_count() * kBlocksPerSm);
-    return launch(w4a16_gemv_kernel<M>, dim3(blocks), dim3(kWarps * 32), 0, st, gp);
+    if (mode == 1) {
+        // register-buffered streaming kernel; at most kBlocksPerSm blocks per SM
+        const int blocks = std::min(strips, sm_count() * kBlocksPerSm);
+        return launch(w4a16_gemv_kernel<M>, dim3(blocks), dim3(kWarps * 32), 0, st, gp);
+    }
+    auto kern = w4a16_tma_kernel<M>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTmaSmem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a16_tma)");
+    const int blocks = std::min((strips + kWarps - 1) / kWarps, sm_count());
+    return launch(kern, dim3(blocks), dim3(kWarps * 32), static_cast<size_t>(kTmaSmem), st, gp);
 }
 
 int run_group(GroupParams& gp, int64_t M, cudaStream_t st) {
@@ -404,6 +531,17 @@ void pack_layout(QF q, ZF z, const uint16_t* scales_gn, int64_t K, int64_t N, in
 }
 
 }  // namespace
+
+unsigned take_w4a16_device_error() {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_w4a16_dev_error, sizeof(v)) != cudaSuccess) return ~0u;
+    if (v) {
+        const unsigned zero = 0;
+        cudaMemcpyToSymbol(g_w4a16_dev_error, &zero, sizeof(zero));
+    }
+    return v;
+}
+
 }  // namespace mcv
 
 using namespace mcv;

@@ -38,6 +38,7 @@ _SIGS = {
     "mcv_set_pdl": [_int],
     "mcv_set_tuning": [_int, _int],
     "mcv_get_tuning": [_int],
+    "mcv_device_errors": [],
     "mcv_w4a16_layout_bytes": [_i64, _i64, _i64, _vp, _vp, _vp],
     "mcv_w4a16_pack_host": [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp],
     "mcv_w4a16_pack_gptq_host": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp],
@@ -67,6 +68,7 @@ _RESTYPE = {
     "mcv_status_string": ctypes.c_char_p,
     "mcv_last_error": ctypes.c_char_p,
     "mcv_set_pdl": None,
+    "mcv_device_errors": ctypes.c_uint,
     "mcv_lm_head_workspace_size": _sz,
     "mcv_nccl_unique_id_bytes": _sz,
     "mcv_lm_head_noalloc_max_bytes": _sz,
@@ -126,6 +128,11 @@ def set_pdl(enabled: bool) -> None:
 
 
 TUNE_W4A16_MODE = 2
+
+
+def device_errors() -> int:
+    """Device-side error bits since the last call (bit 0: a bounded wait gave up)."""
+    return int(lib().mcv_device_errors())
 
 
 def set_tuning(key: int, value: int) -> None:

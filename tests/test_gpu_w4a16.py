@@ -165,10 +165,10 @@ def test_grouped_more_than_one_launch(cuda):
         assert np.array_equal(o.cpu().numpy().view(np.uint16), first.view(np.uint16))
 
 
-@pytest.mark.parametrize("mode", [1, 2])
+@pytest.mark.parametrize("mode", [1, 2, 3])
 @pytest.mark.parametrize("M,K,N", [(1, 1024, 3584), (3, 3584, 1024), (8, 384, 200), (2, 8192, 64)])
 def test_both_kernels_agree(cuda, mode, M, K, N):
-    """The streaming kernel (mode 1) and the K-split kernel (mode 2)."""
+    """Both streaming kernels (modes 1, 3) and the K-split kernel (mode 2)."""
     import mcv_b200
     x, q, z, s = synth.w4a16_inputs(M, K, N, seed=K + N + M)
     w = mcv_b200.pack_w4a16(q, z, s)
@@ -179,3 +179,28 @@ def test_both_kernels_agree(cuda, mode, M, K, N):
     finally:
         mcv_b200.set_tuning(mcv_b200.TUNE_W4A16_MODE, 0)
     assert_f16_close(out, ref, what=f"mode={mode}")
+
+
+def test_grouped_tma_many_problems(cuda):
+    """Enough problems that the default picks the bulk-copy streaming kernel,
+    mixed K (several 512-k chunks per strip) and a ragged N."""
+    import mcv_b200
+    torch = cuda
+    items, refs = [], []
+    for i in range(40):
+        K, N = ((1024, 3584), (3584, 1024), (2048, 1000))[i % 3]
+        x, q, z, s = synth.w4a16_inputs(2, K, N, seed=600 + i)
+        w = mcv_b200.pack_w4a16(q, z, s)
+        items.append((torch.from_numpy(x).cuda(), w, torch.empty((2, N), dtype=torch.float16, device="cuda")))
+        if i < 6:
+            refs.append(oracle.w4a16_gemv(x, oracle.w4a16_fold_zeros(q, z), s, nthreads=8))
+    mcv_b200.matmul_w4a16_grouped(items, M=2)
+    torch.cuda.synchronize()
+    for (x, w, out), ref in zip(items, refs):
+        assert_f16_close(out.cpu().numpy(), ref, what=f"tma grouped K={w.K} N={w.N}")
+
+
+def test_no_device_errors_recorded(cuda):
+    """No bounded wait in any W4A16 kernel gave up during the tests above."""
+    import mcv_b200
+    assert mcv_b200.device_errors() == 0
