@@ -71,18 +71,8 @@ __device__ __forceinline__ void mma_16816(float d[4], const uint32_t a[4], uint3
 
 // One 128-k group for one lane: v[0], v[1] are the lane's weight vectors of
 // the group's two quads, xg points at x[row g][group start + 16t] (read only
-// when g < M).  Returns the group's fp32 sums of x * (q - zero) for rows g,
-// g+8 (columns) x columns 2t, 2t+1 (activation rows).
-//
-// The zero point never enters the inner loop: the magic-number conversion
-// gives 1024+q in the low-nibble lanes (rows g) and 1024+16q in the
-// high-nibble lanes (rows g+8), those go to the MMA as they are, and a second
-// MMA with an all-ones A fragment yields X = sum_k x over the group on the
-// otherwise idle tensor pipe.  Then
-//   rows g   : sum x (q - z) = D - (1024 + z) X
-//   rows g+8 : sum x (q - z) = (D - (1024 + 16 z) X) / 16
-// Products of fp16 values are exact, so the only rounding is fp32
-// accumulation (magnitudes ~1024 |X|, far inside fp32's range).
+// when g < M).  Dequantises and runs 8 MMAs on four independent accumulator
+// chains; returns the group's fp32 sums for rows g, g+8 x columns 2t, 2t+1.
 template <int M>
 __device__ __forceinline__ void group_mma(const uint4 (&v)[2], const __half* xg, int g, int zl_q, int zh_q,
                                           float d[4]) {
@@ -95,9 +85,11 @@ __device__ __forceinline__ void group_mma(const uint4 (&v)[2], const __half* xg,
             xv[qd][1] = *reinterpret_cast<const uint4*>(xg + qd * 64 + 8);
         }
     }
-    constexpr uint32_t kOnes = 0x3c003c00u;  // fp16 1.0 in both lanes
-    const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
-    float cw[2][4] = {}, cx[2][4] = {};
+    const __half z1 = __int2half_rn(1024 + zl_q);   // rows g: 1024 + zero
+    const __half z2 = __int2half_rn(-(64 + zh_q));  // rows g+8: -(64 + zero)
+    const __half2 zl = __halves2half2(z1, z1), zh = __halves2half2(z2, z2);
+    const __half2 inv16 = __halves2half2(__ushort_as_half(0x2c00), __ushort_as_half(0x2c00));
+    float c[4][4] = {};
 #pragma unroll
     for (int kb = 0; kb < 8; ++kb) {
         const int qd = kb >> 2, j = kb & 3;
@@ -109,20 +101,14 @@ __device__ __forceinline__ void group_mma(const uint4 (&v)[2], const __half* xg,
         const uint32_t w8 = w >> 8;
         constexpr uint32_t kMagic = 0x64006400u;
         uint32_t a[4];
-        a[0] = lop3_and_or(w, 0x000f000fu, kMagic);
-        a[1] = lop3_and_or(w, 0x00f000f0u, kMagic);
-        a[2] = lop3_and_or(w8, 0x000f000fu, kMagic);
-        a[3] = lop3_and_or(w8, 0x00f000f0u, kMagic);
-        mma_16816(cw[kb & 1], a, b0, b1);
-        mma_16816(cx[kb & 1], ones, b0, b1);
+        a[0] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w, 0x000f000fu, kMagic)), zl));
+        a[1] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w, 0x00f000f0u, kMagic)), inv16, zh));
+        a[2] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w8, 0x000f000fu, kMagic)), zl));
+        a[3] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w8, 0x00f000f0u, kMagic)), inv16, zh));
+        mma_16816(c[kb & 3], a, b0, b1);
     }
-    const float X0 = cx[0][0] + cx[1][0], X1 = cx[0][1] + cx[1][1];
-    const float zl = 1024.0f + static_cast<float>(zl_q);
-    const float zh = 1024.0f + 16.0f * static_cast<float>(zh_q);
-    d[0] = fmaf(-zl, X0, cw[0][0] + cw[1][0]);
-    d[1] = fmaf(-zl, X1, cw[0][1] + cw[1][1]);
-    d[2] = fmaf(-zh, X0, cw[0][2] + cw[1][2]) * 0.0625f;
-    d[3] = fmaf(-zh, X1, cw[0][3] + cw[1][3]) * 0.0625f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] = (c[0][i] + c[1][i]) + (c[2][i] + c[3][i]);
 }
 
 struct Problem {
@@ -481,7 +467,7 @@ int launch_m(GroupParams& gp, cudaStream_t st) {
         if (per_warp <= 8) return go(w4a16_ksplit_kernel<M, 8>);
         // larger K: the streaming kernel has no K limit
     }
-    if (mode == 1) {
+    if (mode != 3) {
         // register-buffered streaming kernel; at most kBlocksPerSm blocks per SM
         const int blocks = std::min(strips, sm_count() * kBlocksPerSm);
         return launch(w4a16_gemv_kernel<M>, dim3(blocks), dim3(kWarps * 32), 0, st, gp);
