@@ -351,6 +351,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="mcv", choices=["mcv", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip the config 0/2/3 sub-benchmarks")
+    ap.add_argument("--collective", default="p2p", choices=["p2p", "nccl"],
+                    help="N>1: fused peer-mailbox exchange inside the kernel, or a separate NCCL all-reduce")
     ap.add_argument("--profile", choices=["lm_head", "w4a16", "w4a16_grouped", "w8a8"],
                     help="run a few untimed launches of one kernel family (a small case for ncu)")
     ap.add_argument("--rows", type=int, default=65536, help="--profile lm_head: vocab rows (65536 = 128 MB)")
@@ -395,14 +397,23 @@ def main():
     key = torch.empty(1, dtype=torch.int64, device="cuda")
     idx = torch.empty(1, dtype=torch.int64, device="cuda")
     comm = None
-    if world > 1:
+    p2p = None
+    if world > 1 and args.collective == "nccl":
         uid = [mcv.NcclComm.unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, 0)
         comm = mcv.NcclComm(world, rank, uid[0])
+    elif world > 1:
+        p2p = mcv.P2PContext(world, rank)
+        hs = [None] * world
+        dist.all_gather_object(hs, p2p.ipc_handle)
+        p2p.connect(hs)
+        dist.barrier()
 
     def one_step(i):
         w = w_copies[i % copies]
-        if comm is None:
+        if p2p is not None:
+            mcv.lm_head_argmax_p2p(p2p, x, w, ws, key, idx, n_offset=a)
+        elif comm is None:
             mcv.lm_head_argmax(x, w, ws, out_index=idx, out_key=key)
         else:
             mcv.lm_head_argmax_allreduce(comm, x, w, ws, key, idx, n_offset=a)
@@ -449,7 +460,9 @@ def main():
     def e2e_step(i):
         x_dev.copy_(x_host, non_blocking=True)
         w = w_copies[i % copies]
-        if comm is None:
+        if p2p is not None:
+            mcv.lm_head_argmax_p2p(p2p, x_dev, w, ws, key, idx, n_offset=a)
+        elif comm is None:
             mcv.lm_head_argmax(x_dev, w, ws, out_index=idx)
         else:
             mcv.lm_head_argmax_allreduce(comm, x_dev, w, ws, key, idx, n_offset=a)
@@ -514,7 +527,9 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(us_step / 1e3, 6), "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded N(0,0.02) weights)",
             "config": {"workload": WORKLOAD, "K": K_HIDDEN, "vocab": VOCAB, "M": 1, "shard_rows": rows,
-                       "parallelism": f"vocab-shard x{world}" + (" + NCCL allreduce(max) of uint64 key" if world > 1 else ""),
+                       "parallelism": f"vocab-shard x{world}" + (
+                           " + NCCL allreduce(max) of uint64 keys" if comm is not None else
+                           " + in-kernel peer-mailbox exchange of uint64 keys over NVLink" if p2p is not None else ""),
                        "l2": f"inputs larger than L2: {copies} rotating copies of the {shard_bytes / 1e6:.1f} MB shard",
                        "timing": "K steps in one CUDA graph, CUDA events, max over ranks"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
@@ -526,13 +541,21 @@ def main():
                     "d2h_bytes_per_step": 8,
                     "note": "pinned x H2D + C-ABI call + index D2H + stream sync per step"},
             "clocks": clocks,
-            "gpu_launches": args.steps * (1 if world == 1 else 2),
+            "gpu_launches": args.steps * (2 if comm is not None else 1),
         }
         line.update(extras)
         print(json.dumps(line), flush=True)
     if comm is not None:
         torch.cuda.synchronize()
         comm.destroy()
+    if p2p is not None:
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        errs = p2p.errors()
+        if errs:
+            print(f"rank {rank}: peer exchange reported error bits {errs}", file=sys.stderr, flush=True)
+        p2p.destroy()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

@@ -238,6 +238,28 @@ int mcv_lm_head_argmax_allreduce(void* comm, const void* x, const void* w, void*
                                  int64_t n_offset, int fp16_logits, void* workspace,
                                  size_t workspace_bytes, mcv_stream_t stream);
 
+/* ---- sharded lm_head with the reduction fused into the kernel (NVLink) ---- */
+/* Each rank owns a 2 KB mailbox in its HBM and maps every peer's through
+ * CUDA IPC; the last block of each rank's lm_head kernel stores the rank's
+ * argmax keys into all mailboxes (plain release stores over NVLink), waits at
+ * most 1 s for the peers' keys and writes the global first-max index - one
+ * kernel per rank per token, no collective launch.  All ranks must make the
+ * same sequence of calls.  Set-up allocates the mailbox (cudaMalloc); calls
+ * do not allocate.  Replaces the same seam as mcv_lm_head_argmax_allreduce. */
+size_t mcv_p2p_handle_bytes(void);
+/* Creates this rank's context on the current device; writes its IPC handle
+ * (mcv_p2p_handle_bytes() bytes) for the caller to all-gather. */
+int mcv_p2p_create(void** ctx_out, int nranks, int rank, void* handle_out);
+/* Maps the peers' mailboxes; all_handles = nranks handles in rank order. */
+int mcv_p2p_connect(void* ctx, const void* all_handles);
+int mcv_p2p_destroy(void* ctx);
+/* Error bits of this rank since the last call, cleared by it (bit 0: a peer's
+ * key did not arrive within 1 s; that call's out_index is -1).  Synchronous. */
+unsigned mcv_p2p_errors(void* ctx);
+int mcv_lm_head_argmax_p2p(void* ctx, const void* x, const void* w, void* out_key, void* out_index,
+                           int64_t M, int64_t K, int64_t N_shard, int64_t n_offset, int fp16_logits,
+                           void* workspace, size_t workspace_bytes, mcv_stream_t stream);
+
 /* ======================================================================== */
 /* W8A8: int8 activations (per-token absmax) x int8 weights (per channel)   */
 /* ======================================================================== */

@@ -52,6 +52,17 @@ int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStr
 
 int sm_count();
 
+// Cross-GPU exchange of the argmax keys through peer mailboxes (see
+// p2p.cu).  nranks <= 1 disables it.  Mailbox of rank r, in 64-bit words:
+// [parity 2][source rank 8][row 8][key, seq]; written by every rank over
+// NVLink with plain stores, read only by its owner.
+struct P2PArgs {
+    uint64_t* mbox[8];   // mailbox of each rank, as addressable from this GPU
+    uint64_t* seq_dev;   // this rank's call counter (device memory)
+    unsigned* err;       // this rank's error word
+    int rank, nranks;
+};
+
 // Device-side error bits: kernels OR one in when a bounded wait gives up.
 enum : unsigned { kDevErrTimeout = 1u };
 

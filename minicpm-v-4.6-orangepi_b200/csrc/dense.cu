@@ -39,7 +39,25 @@ struct RowArgs {
     int64_t N;
     int K;
     int64_t n_offset;
+    P2PArgs p2p;
 };
+
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
 
 template <int M, int KCH, bool ARGMAX, bool FP16_LOGITS>
 __global__ void __launch_bounds__(kRowThreads)
@@ -160,16 +178,67 @@ rows_kernel(RowArgs a) {
                 if (lane == 0) red[warp][m] = b;
             }
             __syncthreads();
+            __shared__ uint64_t loc[M];
             if (threadIdx.x == 0) {
 #pragma unroll
                 for (int m = 0; m < M; ++m) {
                     uint64_t b = 0;
                     for (int wi = 0; wi < kRowWarps; ++wi) b = red[wi][m] > b ? red[wi][m] : b;
-                    if (a.out_key) a.out_key[m] = b;
-                    if (a.out_index)
-                        a.out_index[m] = static_cast<int64_t>(0xffffffffu - static_cast<uint32_t>(b & 0xffffffffu));
+                    loc[m] = b;
                 }
                 *a.counter = 0u;  // leave the workspace ready for the next call
+            }
+            __syncthreads();
+            if (a.p2p.nranks > 1) {
+                // Exchange: thread j = (r, m) stores this rank's key of row m
+                // into rank r's mailbox, then waits (bounded) for rank j/M's
+                // key of row m in its own mailbox.  Slots alternate by call
+                // parity, so a fast rank's next call never overwrites a slot
+                // a slow rank has yet to read.
+                __shared__ uint64_t got[8][M];
+                const int R = a.p2p.nranks;
+                const uint64_t seq = *a.p2p.seq_dev + 1;
+                const int par = static_cast<int>(seq & 1);
+                const int j = threadIdx.x;
+                if (j < R * M) {
+                    const int r = j / M, m = j % M;
+                    uint64_t* slot = a.p2p.mbox[r] + ((par * 8 + a.p2p.rank) * 8 + m) * 2;
+                    st_relaxed_sys(slot, loc[m]);
+                    st_release_sys(slot + 1, seq);
+                }
+                if (j < R * M) {
+                    const int r = j / M, m = j % M;
+                    const uint64_t* slot = a.p2p.mbox[a.p2p.rank] + ((par * 8 + r) * 8 + m) * 2;
+                    uint64_t key = 0;
+                    const uint64_t t0 = globaltimer_ns();
+                    for (uint32_t spin = 0;; ++spin) {
+                        if (ld_acquire_sys(slot + 1) == seq) {
+                            key = ld_relaxed_sys(slot);
+                            break;
+                        }
+                        if ((spin & 63u) == 63u && globaltimer_ns() - t0 > 1000000000ull) {
+                            atomicOr(a.p2p.err, kDevErrTimeout);  // a peer never arrived
+                            break;
+                        }
+                    }
+                    got[r][m] = key;
+                }
+                __syncthreads();
+                if (threadIdx.x < M) {
+                    const int m = threadIdx.x;
+                    uint64_t b = 0;
+                    for (int r = 0; r < R; ++r) b = got[r][m] > b ? got[r][m] : b;
+                    loc[m] = b;
+                }
+                __syncthreads();
+                if (threadIdx.x == 0) *a.p2p.seq_dev = seq;
+            }
+            if (threadIdx.x < M) {
+                const int m = threadIdx.x;
+                const uint64_t b = loc[m];
+                if (a.out_key) a.out_key[m] = b;
+                if (a.out_index)
+                    a.out_index[m] = b == 0 ? -1 : static_cast<int64_t>(0xffffffffu - static_cast<uint32_t>(b & 0xffffffffu));
             }
         }
     }
@@ -312,10 +381,10 @@ int check_rows(const void* x, const void* w, int64_t M, int64_t K, int64_t N) {
 
 }  // namespace
 
-// Used by the collective entry point in collective.cu.
-int lm_head_argmax_impl(const void* x, const void* w, void* out_key, void* out_index, int64_t M,
-                        int64_t K, int64_t N, int64_t n_offset, int fp16_logits, void* ws,
-                        size_t ws_bytes, cudaStream_t s) {
+// Used by the collective entry points (collective.cu, p2p.cu).
+int lm_head_argmax_impl_p2p(const void* x, const void* w, void* out_key, void* out_index, int64_t M,
+                            int64_t K, int64_t N, int64_t n_offset, int fp16_logits, void* ws,
+                            size_t ws_bytes, cudaStream_t s, const P2PArgs* p2p) {
     int st = check_rows(x, w, M, K, N);
     if (st) return st;
     if (n_offset < 0 || n_offset + N > 0xffffffffLL) return fail(MCV_ERR_SHAPE, "lm_head: global vocab index must fit 32 bits");
@@ -333,7 +402,15 @@ int lm_head_argmax_impl(const void* x, const void* w, void* out_key, void* out_i
     a.N = N;
     a.K = static_cast<int>(K);
     a.n_offset = n_offset;
+    if (p2p) a.p2p = *p2p;
     return fp16_logits ? launch_rows<true, true>(M, a, s, grid) : launch_rows<true, false>(M, a, s, grid);
+}
+
+int lm_head_argmax_impl(const void* x, const void* w, void* out_key, void* out_index, int64_t M,
+                        int64_t K, int64_t N, int64_t n_offset, int fp16_logits, void* ws,
+                        size_t ws_bytes, cudaStream_t s) {
+    return lm_head_argmax_impl_p2p(x, w, out_key, out_index, M, K, N, n_offset, fp16_logits, ws, ws_bytes, s,
+                                   nullptr);
 }
 
 int key_to_index_impl(const void* key, void* out_index, int64_t M, cudaStream_t s) {

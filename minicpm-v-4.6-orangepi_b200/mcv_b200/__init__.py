@@ -58,6 +58,12 @@ _SIGS = {
     "mcv_nccl_comm_init": [_vp, _int, _vp, _int],
     "mcv_nccl_comm_destroy": [_vp],
     "mcv_lm_head_argmax_allreduce": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _sz, _vp],
+    "mcv_p2p_handle_bytes": [],
+    "mcv_p2p_create": [_vp, _int, _int, _vp],
+    "mcv_p2p_connect": [_vp, _vp],
+    "mcv_p2p_destroy": [_vp],
+    "mcv_p2p_errors": [_vp],
+    "mcv_lm_head_argmax_p2p": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _sz, _vp],
     "mcv_w8a8_quantize": [_vp, _vp, _vp, _i64, _i64, _vp],
     "mcv_w8a8_gemm_i32": [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
     "mcv_w8a8_dequant": [_vp, _vp, _vp, _vp, _i64, _i64, _vp],
@@ -71,6 +77,8 @@ _RESTYPE = {
     "mcv_device_errors": ctypes.c_uint,
     "mcv_lm_head_workspace_size": _sz,
     "mcv_nccl_unique_id_bytes": _sz,
+    "mcv_p2p_handle_bytes": _sz,
+    "mcv_p2p_errors": ctypes.c_uint,
     "mcv_lm_head_noalloc_max_bytes": _sz,
 }
 EXPORTED = tuple(_SIGS)
@@ -330,6 +338,38 @@ def lm_head_argmax_allreduce(comm: NcclComm, x, w_shard, workspace, out_key, out
                                               M, K, w_shard.shape[0], n_offset, int(fp16_logits),
                                               _ptr(workspace), workspace.numel(), _stream(stream)),
            "lm_head_argmax_allreduce")
+
+
+class P2PContext:
+    """Peer-mailbox context for the fused sharded lm_head (one per rank)."""
+
+    def __init__(self, nranks: int, rank: int):
+        self.handle = _vp()
+        n = int(lib().mcv_p2p_handle_bytes())
+        buf = ctypes.create_string_buffer(n)
+        _check(lib().mcv_p2p_create(ctypes.byref(self.handle), nranks, rank, buf), "p2p_create")
+        self.ipc_handle = buf.raw
+
+    def connect(self, all_handles) -> None:
+        blob = b"".join(all_handles)
+        _check(lib().mcv_p2p_connect(self.handle, blob), "p2p_connect")
+
+    def errors(self) -> int:
+        return int(lib().mcv_p2p_errors(self.handle))
+
+    def destroy(self) -> None:
+        if self.handle:
+            _check(lib().mcv_p2p_destroy(self.handle), "p2p_destroy")
+            self.handle = _vp()
+
+
+def lm_head_argmax_p2p(ctx: P2PContext, x, w_shard, workspace, out_key, out_index, n_offset: int,
+                       fp16_logits: bool = False, stream=None) -> None:
+    M, K = x.shape
+    _check(lib().mcv_lm_head_argmax_p2p(ctx.handle, _ptr(x), _ptr(w_shard), _ptr(out_key), _ptr(out_index),
+                                        M, K, w_shard.shape[0], n_offset, int(fp16_logits),
+                                        _ptr(workspace), workspace.numel(), _stream(stream)),
+           "lm_head_argmax_p2p")
 
 
 # ---- W8A8 -----------------------------------------------------------------------
