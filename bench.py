@@ -437,11 +437,18 @@ def main():
     if sampler:
         sampler.start()
     # untimed load so clocks settle and the sampler sees the loaded state
-    t_end = time.time() + 1.0
-    while time.time() < t_end:
-        g_warm.replay()
-        torch.cuda.synchronize()
+    # (every rank replays the same number of times: the peer exchange pairs
+    # each rank's n-th call with the others' n-th call)
+    barrier()
+    t0 = time.time()
     g_warm.replay()
+    torch.cuda.synchronize()
+    n_settle = [max(1, min(5000, int(1.0 / max(time.time() - t0, 1e-4))))]
+    if dist is not None:
+        dist.broadcast_object_list(n_settle, 0)
+    for _ in range(n_settle[0]):
+        g_warm.replay()
+    torch.cuda.synchronize()
     barrier()
     ms_main = time_graph_ms(torch, g_main)
     barrier()
