@@ -196,6 +196,9 @@ rows_kernel(RowArgs a) {
                 // parity, so a fast rank's next call never overwrites a slot
                 // a slow rank has yet to read.
                 __shared__ uint64_t got[8][M];
+                __shared__ int failed;
+                if (threadIdx.x == 0) failed = 0;
+                __syncthreads();
                 const int R = a.p2p.nranks;
                 const uint64_t seq = *a.p2p.seq_dev + 1;
                 const int par = static_cast<int>(seq & 1);
@@ -218,6 +221,7 @@ rows_kernel(RowArgs a) {
                         }
                         if ((spin & 63u) == 63u && globaltimer_ns() - t0 > 1000000000ull) {
                             atomicOr(a.p2p.err, kDevErrTimeout);  // a peer never arrived
+                            failed = 1;
                             break;
                         }
                     }
@@ -228,7 +232,7 @@ rows_kernel(RowArgs a) {
                     const int m = threadIdx.x;
                     uint64_t b = 0;
                     for (int r = 0; r < R; ++r) b = got[r][m] > b ? got[r][m] : b;
-                    loc[m] = b;
+                    loc[m] = failed ? 0 : b;  // no answer rather than a partial one
                 }
                 __syncthreads();
                 if (threadIdx.x == 0) *a.p2p.seq_dev = seq;
