@@ -61,8 +61,10 @@ void mcv_set_pdl(int enabled);
  *   MCV_TUNE_W4A16_MODE: 1 = register-buffered streaming kernel (each warp
  *   owns whole 16-column strips), 2 = one block per strip with K split over
  *   its warps (K <= 8192), 3 = streaming kernel fed by warp-private
- *   bulk-copy rings; default: K-split below 4 strips per SM, else 1. */
-enum mcv_tuning_key { MCV_TUNE_W4A16_MODE = 2, MCV_TUNE_COUNT = 8 };
+ *   bulk-copy rings; default: K-split below 4 strips per SM, else 1.
+ *   MCV_TUNE_ROWS_BLOCKS_PER_SM: blocks per SM of the persistent lm_head /
+ *   [N][K] GEMV grid (1..4; default 2). */
+enum mcv_tuning_key { MCV_TUNE_W4A16_MODE = 2, MCV_TUNE_ROWS_BLOCKS_PER_SM = 3, MCV_TUNE_COUNT = 8 };
 int mcv_set_tuning(int key, int value);
 /* Device-side error bits recorded since the last call (and cleared by it):
  * bit 0 = a bounded wait inside a kernel gave up (that kernel returned early

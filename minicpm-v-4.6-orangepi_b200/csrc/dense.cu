@@ -59,94 +59,12 @@ __device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t* p) {
     return v;
 }
 
-template <int M, int KCH, bool ARGMAX, bool FP16_LOGITS>
-__global__ void __launch_bounds__(kRowThreads)
-rows_kernel(RowArgs a) {
-    extern __shared__ uint4 xs[];  // x as [M][K/8] 16-byte chunks
+// Block / grid / (optional) cross-GPU reduction of the argmax keys.  Kept
+// out of line so the streaming loop above is scheduled on its own.
+template <int M>
+__device__ __noinline__ void finish_argmax(const RowArgs& a, const uint64_t (&best)[M], int lane, int warp) {
     __shared__ uint64_t red[kRowWarps][M];
     __shared__ int is_last;
-
-    const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
-    const int chunks = a.K >> 3;
-    const int64_t gwarp = static_cast<int64_t>(blockIdx.x) * kRowWarps + warp;
-    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kRowWarps;
-    const uint4* w4 = reinterpret_cast<const uint4*>(a.w);
-
-    // Prefetch this warp's first rows before waiting on the previous kernel.
-    uint4 wv[kRowsPerStep][KCH];
-    int64_t r = gwarp * kRowsPerStep;
-    const int64_t step = nwarps * kRowsPerStep;
-#pragma unroll
-    for (int t = 0; t < kRowsPerStep; ++t)
-#pragma unroll
-        for (int i = 0; i < KCH; ++i) {
-            const int c = lane + 32 * i;
-            if (r + t < a.N && c < chunks) wv[t][i] = ld_stream(w4 + (r + t) * chunks + c);
-        }
-    pdl_trigger();
-    pdl_wait();
-    for (int idx = threadIdx.x; idx < M * chunks; idx += kRowThreads)
-        xs[idx] = reinterpret_cast<const uint4*>(a.x)[idx];
-    __syncthreads();
-
-    uint64_t best[M];
-#pragma unroll
-    for (int m = 0; m < M; ++m) best[m] = 0;
-
-    while (r < a.N) {
-        float acc0[kRowsPerStep][M], acc1[kRowsPerStep][M];
-#pragma unroll
-        for (int t = 0; t < kRowsPerStep; ++t)
-#pragma unroll
-            for (int m = 0; m < M; ++m) acc0[t][m] = acc1[t][m] = 0.0f;
-#pragma unroll
-        for (int i = 0; i < KCH; ++i) {
-            const int c = lane + 32 * i;
-            if (c < chunks) {
-#pragma unroll
-                for (int m = 0; m < M; ++m) {
-                    const uint4 xv = xs[m * chunks + c];
-#pragma unroll
-                    for (int t = 0; t < kRowsPerStep; ++t) {
-                        fma2_f16_f32(acc0[t][m], acc1[t][m], wv[t][i].x, xv.x);
-                        fma2_f16_f32(acc0[t][m], acc1[t][m], wv[t][i].y, xv.y);
-                        fma2_f16_f32(acc0[t][m], acc1[t][m], wv[t][i].z, xv.z);
-                        fma2_f16_f32(acc0[t][m], acc1[t][m], wv[t][i].w, xv.w);
-                    }
-                }
-            }
-        }
-        // issue the next step's loads before reducing this one
-        const int64_t rn = r + step;
-#pragma unroll
-        for (int t = 0; t < kRowsPerStep; ++t)
-#pragma unroll
-            for (int i = 0; i < KCH; ++i) {
-                const int c = lane + 32 * i;
-                if (rn + t < a.N && c < chunks) wv[t][i] = ld_stream(w4 + (rn + t) * chunks + c);
-            }
-#pragma unroll
-        for (int t = 0; t < kRowsPerStep; ++t) {
-            const int64_t row = r + t;
-#pragma unroll
-            for (int m = 0; m < M; ++m) {
-                float v = warp_sum(acc0[t][m] + acc1[t][m]);
-                if (row < a.N) {
-                    if constexpr (ARGMAX) {
-                        if constexpr (FP16_LOGITS) v = __half2float(__float2half_rn(v));
-                        const uint64_t key = argmax_key(v, static_cast<uint32_t>(a.n_offset + row));
-                        best[m] = key > best[m] ? key : best[m];
-                    } else {
-                        if (lane == m) a.out[static_cast<int64_t>(m) * a.N + row] = __float2half_rn(v);
-                    }
-                }
-            }
-        }
-        r = rn;
-    }
-
-    if constexpr (ARGMAX) {
         // keys are already warp-uniform (butterfly reduction)
         if (lane == 0) {
 #pragma unroll
@@ -245,7 +163,93 @@ rows_kernel(RowArgs a) {
                     a.out_index[m] = b == 0 ? -1 : static_cast<int64_t>(0xffffffffu - static_cast<uint32_t>(b & 0xffffffffu));
             }
         }
+}
+
+template <int M, int KCH, bool ARGMAX, bool FP16_LOGITS>
+__global__ void __launch_bounds__(kRowThreads)
+rows_kernel(RowArgs a) {
+    extern __shared__ uint4 xs[];  // x as [M][K/8] 16-byte chunks
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int chunks = a.K >> 3;
+    const int64_t gwarp = static_cast<int64_t>(blockIdx.x) * kRowWarps + warp;
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kRowWarps;
+    const uint4* w4 = reinterpret_cast<const uint4*>(a.w);
+
+    // Prefetch this warp's first rows before waiting on the previous kernel.
+    uint4 wv[kRowsPerStep][KCH];
+    int64_t r = gwarp * kRowsPerStep;
+    const int64_t step = nwarps * kRowsPerStep;
+#pragma unroll
+    for (int t = 0; t < kRowsPerStep; ++t)
+#pragma unroll
+        for (int i = 0; i < KCH; ++i) {
+            const int c = lane + 32 * i;
+            if (r + t < a.N && c < chunks) wv[t][i] = ld_stream(w4 + (r + t) * chunks + c);
+        }
+    pdl_trigger();
+    pdl_wait();
+    for (int idx = threadIdx.x; idx < M * chunks; idx += kRowThreads)
+        xs[idx] = reinterpret_cast<const uint4*>(a.x)[idx];
+    __syncthreads();
+
+    uint64_t best[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) best[m] = 0;
+
+    while (r < a.N) {
+        float acc0[kRowsPerStep][M], acc1[kRowsPerStep][M];
+#pragma unroll
+        for (int t = 0; t < kRowsPerStep; ++t)
+#pragma unroll
+            for (int m = 0; m < M; ++m) acc0[t][m] = acc1[t][m] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < KCH; ++i) {
+            const int c = lane + 32 * i;
+            if (c < chunks) {
+#pragma unroll
+                for (int m = 0; m < M; ++m) {
+                    const uint4 xv = xs[m * chunks + c];
+#pragma unroll
+                    for (int t = 0; t < kRowsPerStep; ++t) {
+                        fma2_f16_f32(acc0[t][m], acc1[t][m], wv[t][i].x, xv.x);
+                        fma2_f16_f32(acc0[t][m], acc1[t][m], wv[t][i].y, xv.y);
+                        fma2_f16_f32(acc0[t][m], acc1[t][m], wv[t][i].z, xv.z);
+                        fma2_f16_f32(acc0[t][m], acc1[t][m], wv[t][i].w, xv.w);
+                    }
+                }
+            }
+        }
+        // issue the next step's loads before reducing this one
+        const int64_t rn = r + step;
+#pragma unroll
+        for (int t = 0; t < kRowsPerStep; ++t)
+#pragma unroll
+            for (int i = 0; i < KCH; ++i) {
+                const int c = lane + 32 * i;
+                if (rn + t < a.N && c < chunks) wv[t][i] = ld_stream(w4 + (rn + t) * chunks + c);
+            }
+#pragma unroll
+        for (int t = 0; t < kRowsPerStep; ++t) {
+            const int64_t row = r + t;
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                float v = warp_sum(acc0[t][m] + acc1[t][m]);
+                if (row < a.N) {
+                    if constexpr (ARGMAX) {
+                        if constexpr (FP16_LOGITS) v = __half2float(__float2half_rn(v));
+                        const uint64_t key = argmax_key(v, static_cast<uint32_t>(a.n_offset + row));
+                        best[m] = key > best[m] ? key : best[m];
+                    } else {
+                        if (lane == m) a.out[static_cast<int64_t>(m) * a.N + row] = __float2half_rn(v);
+                    }
+                }
+            }
+        }
+        r = rn;
     }
+
+    if constexpr (ARGMAX) finish_argmax<M>(a, best, lane, warp);
 }
 
 // [K][N] natural layout: each thread owns 8 consecutive columns (one 16-byte
@@ -333,7 +337,9 @@ int row_grid(int64_t N) {
     // blocks than there are row pairs to hand out
     const int64_t warps_needed = (N + kRowsPerStep - 1) / kRowsPerStep;
     const int64_t blocks_needed = (warps_needed + kRowWarps - 1) / kRowWarps;
-    const int64_t cap = static_cast<int64_t>(sm_count()) * 4;
+    const int t = tuning(MCV_TUNE_ROWS_BLOCKS_PER_SM);
+    const int bps = (t >= 1 && t <= 4) ? t : 2;  // <= 4: the workspace is sized for 4 blocks per SM
+    const int64_t cap = static_cast<int64_t>(sm_count()) * bps;
     return static_cast<int>(blocks_needed < cap ? blocks_needed : cap);
 }
 
