@@ -552,8 +552,13 @@ def main():
         }
         line.update(extras)
         print(json.dumps(line), flush=True)
+    # graphs hold captured collective launches: release them before the
+    # communicator and the mailboxes they refer to
+    del g_warm, g_main, g_kern
+    torch.cuda.synchronize()
     if comm is not None:
-        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
         comm.destroy()
     if p2p is not None:
         torch.cuda.synchronize()
