@@ -212,8 +212,8 @@ int mcv_argmax_last_dim_f16(const void* logits, void* out_index, int64_t M, int6
  * large enough for every supported M (1..8), and larger requests are rejected
  * with MCV_ERR_WORKSPACE.  The first call on a device looks up the array's
  * device address (cudaGetSymbolAddress), so make that first call before any
- * stream capture.  Each call clears the array's header with cudaMemsetAsync on
- * `stream` and allocates nothing.  All calls share the one array: calls that
+ * stream capture.  Each call clears the array with cudaMemsetAsync on `stream` and
+ * allocates nothing.  All calls share the one array: calls that
  * may overlap on the GPU (other streams, other threads) race and must be
  * serialised by the caller. */
 size_t mcv_lm_head_noalloc_max_bytes(void);

@@ -17,8 +17,9 @@
 // rows per warp per step.  In argmax mode each logit becomes a 64-bit
 // order-preserving key (larger logit wins, then smaller index) so the whole
 // reduction is an integer max: per warp in registers, per block in shared
-// memory, and across blocks by the last block to finish (a counter in the
-// caller's workspace, reset by that block so the next call needs no memset).
+// memory, and across blocks through a 64-bit atomicMax per row and an
+// arrival counter in the caller's workspace; the last block to arrive reads
+// the result and zeroes both, so the next call needs no memset.
 #include "common.cuh"
 
 namespace mcv {
@@ -28,12 +29,21 @@ constexpr int kRowThreads = 256;
 constexpr int kRowWarps = kRowThreads / 32;
 constexpr int kRowsPerStep = 2;
 
+static __device__ unsigned g_dense_dev_error;
+constexpr int kPrefetchSteps = 3;  // row steps per warp warmed into L2 before the PDL wait
+
+// L2 prefetch of a contiguous range of this GPU's memory (16-byte aligned,
+// size a multiple of 16; no multicast).
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 struct RowArgs {
     const __half* x;
     const __half* w;
     __half* out;            // GEMV mode
-    uint64_t* partial;      // argmax: [gridDim.x][M]
-    unsigned* counter;      // argmax: blocks finished
+    unsigned* counter;      // argmax: blocks arrived (zero between calls)
+    uint64_t* keys;         // argmax: [M] running maxima (zero between calls)
     uint64_t* out_key;      // argmax: [M] (may be null)
     int64_t* out_index;     // argmax: [M] (may be null)
     int64_t N;
@@ -64,47 +74,37 @@ __device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t* p) {
 template <int M>
 __device__ __noinline__ void finish_argmax(const RowArgs& a, const uint64_t (&best)[M], int lane, int warp) {
     __shared__ uint64_t red[kRowWarps][M];
-    __shared__ int is_last;
-        // keys are already warp-uniform (butterfly reduction)
+        // keys are already warp-uniform (butterfly reduction).  Blocks fold
+        // their key into one global key per row with a 64-bit atomicMax and
+        // arrive on a counter with acquire-release order; the last block to
+        // arrive reads the final keys and resets both for the next call.
         if (lane == 0) {
 #pragma unroll
             for (int m = 0; m < M; ++m) red[warp][m] = best[m];
         }
         __syncthreads();
+        __shared__ int is_last;
         if (threadIdx.x == 0) {
 #pragma unroll
             for (int m = 0; m < M; ++m) {
                 uint64_t b = 0;
                 for (int wi = 0; wi < kRowWarps; ++wi) b = red[wi][m] > b ? red[wi][m] : b;
-                a.partial[static_cast<int64_t>(blockIdx.x) * M + m] = b;
+                atomicMax(reinterpret_cast<unsigned long long*>(a.keys + m), static_cast<unsigned long long>(b));
             }
-            __threadfence();
-            const unsigned prev = atomicAdd(a.counter, 1u);
+            unsigned prev;
+            asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(a.counter) : "memory");
             is_last = (prev == gridDim.x - 1);
         }
         __syncthreads();
         if (is_last) {
-            __threadfence();
-#pragma unroll
-            for (int m = 0; m < M; ++m) {
-                uint64_t b = 0;
-                for (int blk = threadIdx.x; blk < static_cast<int>(gridDim.x); blk += kRowThreads) {
-                    const uint64_t v = __ldcg(a.partial + static_cast<int64_t>(blk) * M + m);
-                    b = v > b ? v : b;
-                }
-                b = warp_max_u64(b);
-                if (lane == 0) red[warp][m] = b;
-            }
-            __syncthreads();
             __shared__ uint64_t loc[M];
             if (threadIdx.x == 0) {
 #pragma unroll
                 for (int m = 0; m < M; ++m) {
-                    uint64_t b = 0;
-                    for (int wi = 0; wi < kRowWarps; ++wi) b = red[wi][m] > b ? red[wi][m] : b;
-                    loc[m] = b;
+                    loc[m] = __ldcg(a.keys + m);
+                    a.keys[m] = 0;  // leave the workspace ready for the next call
                 }
-                *a.counter = 0u;  // leave the workspace ready for the next call
+                *a.counter = 0u;
             }
             __syncthreads();
             if (a.p2p.nranks > 1) {
@@ -187,6 +187,13 @@ rows_kernel(RowArgs a) {
             const int c = lane + 32 * i;
             if (r + t < a.N && c < chunks) wv[t][i] = ld_stream(w4 + (r + t) * chunks + c);
         }
+    // Warm L2 with this warp's next few row pairs too (bulk prefetch, no
+    // registers): the weights never depend on the previous kernel, so their
+    // stream can start before griddepcontrol.wait releases.
+    if (lane < kRowsPerStep * kPrefetchSteps) {
+        const int64_t pr = r + step * (1 + lane / kRowsPerStep) + (lane % kRowsPerStep);
+        if (pr < a.N) prefetch_l2(w4 + pr * chunks, static_cast<uint32_t>(a.K) * 2u);
+    }
     pdl_trigger();
     pdl_wait();
     for (int idx = threadIdx.x; idx < M * chunks; idx += kRowThreads)
@@ -406,7 +413,7 @@ int lm_head_argmax_impl_p2p(const void* x, const void* w, void* out_key, void* o
     a.x = static_cast<const __half*>(x);
     a.w = static_cast<const __half*>(w);
     a.counter = static_cast<unsigned*>(ws);
-    a.partial = reinterpret_cast<uint64_t*>(static_cast<char*>(ws) + 256);
+    a.keys = reinterpret_cast<uint64_t*>(static_cast<char*>(ws) + 64);
     a.out_key = static_cast<uint64_t*>(out_key);
     a.out_index = static_cast<int64_t*>(out_index);
     a.N = N;
@@ -414,6 +421,16 @@ int lm_head_argmax_impl_p2p(const void* x, const void* w, void* out_key, void* o
     a.n_offset = n_offset;
     if (p2p) a.p2p = *p2p;
     return fp16_logits ? launch_rows<true, true>(M, a, s, grid) : launch_rows<true, false>(M, a, s, grid);
+}
+
+unsigned take_dense_device_error() {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_dense_dev_error, sizeof(v)) != cudaSuccess) return ~0u;
+    if (v) {
+        const unsigned zero = 0;
+        cudaMemcpyToSymbol(g_dense_dev_error, &zero, sizeof(zero));
+    }
+    return v;
 }
 
 int lm_head_argmax_impl(const void* x, const void* w, void* out_key, void* out_index, int64_t M,
@@ -480,9 +497,9 @@ int mcv_gemv_f16(const void* x, const void* w, void* out, int64_t M, int64_t K, 
 
 size_t mcv_lm_head_workspace_size(int64_t M) {
     if (M < 1) M = 1;
-    // 256 B header (the block counter) + one key per (block, row); the grid is
-    // at most 4 blocks per SM, sized here for parts with up to 1024 SMs.
-    return 256 + static_cast<size_t>(4 * 1024) * static_cast<size_t>(M) * sizeof(uint64_t);
+    // a 64-byte counter slot and one 64-bit key per row, in a 256-byte header
+    (void)M;
+    return 256;
 }
 
 int mcv_lm_head_argmax(const void* x, const void* w, void* out_key, void* out_index, int64_t M, int64_t K,

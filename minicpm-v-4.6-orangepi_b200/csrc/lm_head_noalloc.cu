@@ -19,9 +19,9 @@ int lm_head_argmax_impl(const void* x, const void* w, void* out_key, void* out_i
 
 namespace {
 
-// Large enough for mcv_lm_head_workspace_size(8): a 256-byte header plus one
-// key per (block, row) for up to 4096 blocks and 8 rows.
-constexpr size_t kNoAllocBytes = 256 + 4096 * 8 * sizeof(uint64_t);
+// Large enough for mcv_lm_head_workspace_size(M) for every supported M: an
+// arrival counter and one 64-bit running key per row.
+constexpr size_t kNoAllocBytes = 256;
 
 static __device__ __align__(256) unsigned char g_lm_head_scratch[kNoAllocBytes];
 
@@ -68,10 +68,10 @@ int mcv_lm_head_argmax_noalloc(const void* x, const void* w, void* out_key, void
     int st = scratch_for_current_device(&ws);
     if (st) return st;
     auto s = static_cast<cudaStream_t>(stream);
-    // The array keeps whatever the previous call left; the block counter in
-    // its header must start at zero.
-    cudaError_t e = cudaMemsetAsync(ws, 0, 256, s);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(lm_head scratch header)");
+    // The array keeps whatever the previous call left; its counter and
+    // running keys must be zero when a call begins.
+    cudaError_t e = cudaMemsetAsync(ws, 0, kNoAllocBytes, s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(lm_head scratch)");
     return lm_head_argmax_impl(x, w, out_key, out_index, M, K, N_shard, n_offset, fp16_logits, ws, kNoAllocBytes, s);
 }
 
