@@ -145,6 +145,17 @@ int mcv_w4a16_gemv(const void* x, const void* qweight, const void* scales, const
                    int zero_bias, void* out, int64_t M, int64_t K, int64_t N, int64_t group,
                    mcv_stream_t stream);
 
+/* out[m][n] = sum_k x[m][k] * w[k][n] for larger M (batched decode, prefill;
+ * intended for M >= 16), on the tcgen05 tensor cores: x tiles by TMA, int4
+ * weights dequantised to fp16 (q - zero) * scale in shared memory, fp32
+ * accumulation in tensor memory, fp16 out.  Same mcv-int4 weights as
+ * mcv_w4a16_gemv; group 128; x and qweight 16-byte aligned; K a multiple of
+ * 128.  The reference has no quantized GEMM for M > 1: it runs prefill through
+ * matmul_b_transposed's dense path (src/csrc/lib/ops.cpp:215-322). */
+int mcv_w4a16_gemm(const void* x, const void* qweight, const void* scales, const void* zeros,
+                   int zero_bias, void* out, int64_t M, int64_t K, int64_t N, int64_t group,
+                   mcv_stream_t stream);
+
 /* Several independent W4A16 GEMVs (same M) in one launch: problems is a HOST
  * array; each entry's x/out/weights are device pointers.  No problem may read
  * another problem's output.  For projections that share an input (q/k/v,

@@ -46,6 +46,7 @@ _SIGS = {
     "mcv_w4a16_pack_from_tiles_host": [_vp, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _vp],
     "mcv_w4a16_gemv": [_vp, _vp, _vp, _vp, _int, _vp, _i64, _i64, _i64, _i64, _vp],
     "mcv_w4a16_gemv_grouped": [_vp, _int, _i64, _vp],
+    "mcv_w4a16_gemm": [_vp, _vp, _vp, _vp, _int, _vp, _i64, _i64, _i64, _i64, _vp],
     "mcv_gemv_f16": [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
     "mcv_lm_head_workspace_size": [_i64],
     "mcv_lm_head_argmax": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _sz, _vp],
@@ -245,6 +246,13 @@ def matmul_w4a16(x, w: W4A16QuantizedWeight, out, stream=None) -> None:
     M = x.shape[0] if x.dim() == 2 else 1
     _check(lib().mcv_w4a16_gemv(_ptr(x), _ptr(w.qweight), _ptr(w.scales), _ptr(w.zeros), w.zero_bias, _ptr(out),
                                 M, w.K, w.N, w.group_size, _stream(stream)), "matmul_w4a16")
+
+
+def matmul_w4a16_gemm(x, w: W4A16QuantizedWeight, out, stream=None) -> None:
+    """out fp16 [M,N] = x fp16 [M,K] @ dequant(w) on the tcgen05 tensor cores (M >= 16)."""
+    M = x.shape[0]
+    _check(lib().mcv_w4a16_gemm(_ptr(x), _ptr(w.qweight), _ptr(w.scales), _ptr(w.zeros), w.zero_bias, _ptr(out),
+                                M, w.K, w.N, w.group_size, _stream(stream)), "matmul_w4a16_gemm")
 
 
 class W4A16Problem(ctypes.Structure):
