@@ -242,6 +242,42 @@ def bench_w8a8(torch, mcv, synth, l2, hbm):
     return {"config": "config2 fused quantize+int8 GEMV+dequant, K=1024, weights [N][K]", "cases": res}
 
 
+def bench_w4a16_gemm(torch, mcv, synth, l2, hbm, tflops):
+    """Config 4: W4A16 GEMM on the tcgen05 path, M in {16,64,256,1024},
+    K=1024, N in {3584,4096}.  Weight copies rotate past 2x L2 for the small,
+    HBM-bound M; bound = max(bytes / HBM peak, flops / tensor peak)."""
+    res = []
+    K = 1024
+    for N in (3584, 4096):
+        _, q, z, s = synth.w4a16_inputs(1, K, N, seed=N)
+        w0 = mcv.pack_w4a16(q, z, s)
+        copies = max(2, int(np.ceil(2 * l2 / w0.nbytes)))
+        ws = [w0] + [mcv.W4A16QuantizedWeight(w0.qweight.clone(), w0.scales.clone(), w0.zeros.clone(), 0, K, N)
+                     for _ in range(copies - 1)]
+        for M in (16, 64, 256, 1024):
+            x = torch.randn((M, K), device="cuda").to(torch.float16)
+            out = torch.empty((M, N), dtype=torch.float16, device="cuda")
+
+            def step():
+                for w in ws:
+                    mcv.matmul_w4a16_gemm(x, w, out)
+            step()
+            torch.cuda.synchronize()
+            g = graph_of(torch, step, torch.cuda.Stream())
+            g.replay()
+            torch.cuda.synchronize()
+            us = time_graph_ms(torch, g, reps=5) / copies * 1e3
+            flops = 2.0 * M * N * K
+            byts = synth.w4a16_bytes(M, K, N)
+            t_roof = max(byts / (hbm * 1e3), flops / (tflops * 1e6))  # us
+            res.append({"M": M, "N": N, "us": round(us, 3), "TFLOPs": round(flops / (us * 1e-6) / 1e12, 2),
+                        "GBps": round(byts / (us * 1e-6) / 1e9, 1), "roofline_us": round(t_roof, 3),
+                        "frac_of_roofline": round(t_roof / us, 4)})
+            del g
+        del ws
+    return {"config": "config4 W4A16 GEMM, tcgen05.mma kind::f16, fp32 accumulation in TMEM, K=1024", "cases": res}
+
+
 def bench_decode_step(torch, mcv, synth, hbm, lm_w, ws_lm):
     """Config 3: the 186 projections of one token + the lm_head.  'separate'
     launches each projection on its own (the reference's call pattern);
@@ -332,6 +368,13 @@ def run_profile(args):
         probs = mcv.w4a16_problems(list(zip([xd] * 48, ws, outs)))
         for _ in range(5):
             mcv.matmul_w4a16_grouped(None, problems=probs)
+    elif args.profile == "gemm":
+        _, q, z, s = synth.w4a16_inputs(1, 1024, 4096, seed=4096)
+        w = mcv.pack_w4a16(q, z, s)
+        x = torch.randn((1024, 1024), device="cuda").to(torch.float16)
+        out = torch.empty((1024, 4096), dtype=torch.float16, device="cuda")
+        for _ in range(5):
+            mcv.matmul_w4a16_gemm(x, w, out)
     elif args.profile == "w8a8":
         for M in (1, 8):
             x, w8, ws8 = synth.w8a8_inputs(M, 1024, 3584, seed=2)
@@ -353,7 +396,7 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the config 0/2/3 sub-benchmarks")
     ap.add_argument("--collective", default="p2p", choices=["p2p", "nccl"],
                     help="N>1: fused peer-mailbox exchange inside the kernel, or a separate NCCL all-reduce")
-    ap.add_argument("--profile", choices=["lm_head", "w4a16", "w4a16_grouped", "w8a8"],
+    ap.add_argument("--profile", choices=["lm_head", "w4a16", "w4a16_grouped", "w8a8", "gemm"],
                     help="run a few untimed launches of one kernel family (a small case for ncu)")
     ap.add_argument("--rows", type=int, default=65536, help="--profile lm_head: vocab rows (65536 = 128 MB)")
     args = ap.parse_args()
@@ -521,6 +564,7 @@ def main():
             extras["w4a16_gemv"] = bench_w4a16_gemv(torch, mcv, synth, l2, hbm)
             extras["w8a8"] = bench_w8a8(torch, mcv, synth, l2, hbm)
             extras["decode_step"] = bench_decode_step(torch, mcv, synth, hbm, w_copies[0], ws)
+            extras["w4a16_gemm"] = bench_w4a16_gemm(torch, mcv, synth, l2, hbm, _tf)
 
     if rank == 0:
         algo_bytes = rows * K_HIDDEN * 2 + K_HIDDEN * 2 + 8
