@@ -14,8 +14,9 @@
 //    consecutive k of two columns - to fp16 (q - zero) * scale and store them
 //    in the same 128-byte-swizzled K-major layout;
 //  * one thread issues four tcgen05.mma.kind::f16 (M=128, N=128, K=16) per
-//    64-k stage and commits them to an mbarrier; two stages double-buffer so
-//    the dequantisation of stage i+1 overlaps the MMAs of stage i;
+//    64-k stage and commits them to an mbarrier; a 4-stage shared-memory ring
+//    keeps x tiles two stages ahead (TMA) and weight vectors two stages ahead
+//    (registers), so copies and dequantisation overlap the MMAs;
 //  * the epilogue reads the accumulator with tcgen05.ld (warp w owns TMEM
 //    lanes 32w..32w+31 = rows) and writes fp16.
 // Every wait is bounded (2 s); on a timeout the block records an error bit,
@@ -38,7 +39,8 @@ constexpr int kBN = 128;         // output columns per block (MMA N)
 constexpr int kBK = 64;          // k per stage: one 128-byte swizzle row
 constexpr int kThreads = 256;
 constexpr int kTileBytes = kBM * kBK * 2;  // 16 KB (both operands)
-constexpr int kSmemBytes = 2 * 2 * kTileBytes + 1024 + 256;
+constexpr int kStages = 4;                 // smem ring depth (x tile + weight tile per stage)
+constexpr int kSmemBytes = kStages * 2 * kTileBytes + 1024 + 256;
 
 static __device__ unsigned g_gemm_dev_error;
 
@@ -157,12 +159,12 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
     extern __shared__ unsigned char smem_raw[];
     // 1024-byte alignment for the swizzle atoms
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    // x tiles at [0, 32K), weight tiles at [32K, 64K)
+    // x tiles, then weight tiles, one of each per ring stage
     auto xt = [&](int b) { return smem + b * kTileBytes; };
-    auto wt = [&](int b) { return smem + (2 + b) * kTileBytes; };
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + 4 * kTileBytes);  // [2]
-    uint64_t* done = full + 2;                                              // [2]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 2);
+    auto wt = [&](int b) { return smem + (kStages + b) * kTileBytes; };
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * kStages * kTileBytes);  // [kStages]
+    uint64_t* done = full + kStages;                                                  // [kStages]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + kStages);
     volatile int* failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -178,7 +180,7 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 0) {
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < kStages; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&done[i], 1);
         }
@@ -203,17 +205,36 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
 
     pdl_trigger();
     pdl_wait();  // x may be the previous kernel's output
-    if (tid == 0) {
-        mbar_expect_tx(&full[0], kTileBytes);
-        tma_load_2d(xt(0), &xmap, 0, m0, &full[0]);
-    }
+    // x tiles run kAhead stages ahead of the MMAs: stage j goes into ring slot
+    // j % kStages once the MMAs of stage j - kStages (two stages before the
+    // current one) have released it, so the producer never waits on the
+    // MMAs it has just issued.  Weight vectors are prefetched two stages
+    // ahead in registers.
+    constexpr int kAhead = kStages - 2;
+    auto issue_x = [&](int j) {
+        const int sj = j % kStages;
+        mbar_expect_tx(&full[sj], kTileBytes);
+        tma_load_2d(xt(sj), &xmap, j * kBK, m0, &full[sj]);
+    };
+    if (tid == 0)
+        for (int j = 0; j < kAhead && j < nst; ++j) issue_x(j);
     uint4 cur = load_vec(0);
+    uint4 nx1 = nst > 1 ? load_vec(1) : make_uint4(0, 0, 0, 0);
     bool ok = true;
     for (int i = 0; i < nst && ok; ++i) {
-        const int b = i & 1;
-        // tile b was last read by the MMAs of stage i-2
-        if (i >= 2 && !mbar_wait(&done[b], static_cast<uint32_t>((i - 2) >> 1) & 1u)) ok = false;
-        const uint4 nxt = (i + 1 < nst) ? load_vec(i + 1) : make_uint4(0, 0, 0, 0);
+        const int b = i % kStages;
+        const uint32_t ph = static_cast<uint32_t>(i / kStages) & 1u;
+        // refill: stage i + kAhead reuses the slot of stage i + kAhead - kStages = i - 2
+        if (tid == 0 && i + kAhead < nst) {
+            const int j = i + kAhead;
+            if (j >= kStages && !mbar_wait(&done[j % kStages], static_cast<uint32_t>((j - kStages) / kStages) & 1u))
+                *failed = 1;
+            else
+                issue_x(j);
+        }
+        const uint4 nx2 = (i + 2 < nst) ? load_vec(i + 2) : make_uint4(0, 0, 0, 0);
+        // weight tile b was last read by the MMAs of stage i - kStages
+        if (i >= kStages && !mbar_wait(&done[b], ph ^ 1u)) ok = false;
         if (ok) {
             const int grp = (i * kBK) / 128;
             int zl = 0, zh = 0;
@@ -228,7 +249,7 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
         }
         // make the generic-proxy stores visible to the tensor core
         fence_proxy_async_smem();
-        if (ok && !mbar_wait(&full[b], static_cast<uint32_t>(i >> 1) & 1u)) ok = false;
+        if (ok && !mbar_wait(&full[b], ph)) ok = false;
         if (!ok) *failed = 1;
         tc_fence_before();
         __syncthreads();
@@ -245,28 +266,22 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
                 mma_f16(tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
             }
             mma_commit(&done[b]);
-            // refill the other x buffer once the MMAs of stage i-1 are done
-            if (i + 1 < nst) {
-                if (i >= 1 && !mbar_wait(&done[b ^ 1], static_cast<uint32_t>((i - 1) >> 1) & 1u)) {
-                    *failed = 1;
-                } else {
-                    mbar_expect_tx(&full[b ^ 1], kTileBytes);
-                    tma_load_2d(xt(b ^ 1), &xmap, (i + 1) * kBK, m0, &full[b ^ 1]);
-                }
-            }
         }
-        cur = nxt;
+        cur = nx1;
+        nx1 = nx2;
     }
     // accumulator complete once the last stage's MMAs are
     bool acc_ready = false;
-    if (ok && !*failed) acc_ready = mbar_wait(&done[(nst - 1) & 1], static_cast<uint32_t>((nst - 1) >> 1) & 1u);
+    if (ok && !*failed)
+        acc_ready = mbar_wait(&done[(nst - 1) % kStages], static_cast<uint32_t>((nst - 1) / kStages) & 1u);
     if (!acc_ready) {
         atomicOr(&g_gemm_dev_error, kDevErrTimeout);
         // give issued MMAs (bounded) time to finish before freeing their memory
-        for (int s = 0; s < 2 && s < nst; ++s) {
-            const int last = ((nst - 1) & 1) == s ? nst - 1 : nst - 2;
-            if (last >= 0) mbar_wait(&done[s], static_cast<uint32_t>(last >> 1) & 1u);
-        }
+        if (tid == 0)
+            for (int s = 0; s < kStages && s < nst; ++s) {
+                const int last = s + ((nst - 1 - s) / kStages) * kStages;  // last stage that used slot s
+                mbar_wait(&done[s], static_cast<uint32_t>(last / kStages) & 1u);
+            }
     }
     tc_fence_after();
     if (acc_ready && warp < 4) {
