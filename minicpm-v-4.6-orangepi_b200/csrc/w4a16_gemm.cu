@@ -218,8 +218,27 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
     };
     if (tid == 0)
         for (int j = 0; j < kAhead && j < nst; ++j) issue_x(j);
-    uint4 cur = load_vec(0);
-    uint4 nx1 = nst > 1 ? load_vec(1) : make_uint4(0, 0, 0, 0);
+    // per-stage operands of this thread: its weight vector plus the scale and
+    // zero of its two columns for the stage's 128-k group
+    struct Ops {
+        uint4 v;
+        uint32_t zlo, zhi;
+        unsigned short slo, shi;
+    };
+    auto load_ops = [&](int i) -> Ops {
+        Ops o{make_uint4(0, 0, 0, 0), 0u, 0u, 0, 0};
+        if (i < nst && have_strip) {
+            o.v = load_vec(i);
+            const int grp = (i * kBK) / 128;
+            o.zlo = a.z[static_cast<size_t>(col) * zw + (grp >> 3)] >> (4 * (grp & 7));
+            o.zhi = a.z[static_cast<size_t>(col + 8) * zw + (grp >> 3)] >> (4 * (grp & 7));
+            o.slo = __half_as_ushort(a.s[static_cast<size_t>(col) * Gp + grp]);
+            o.shi = __half_as_ushort(a.s[static_cast<size_t>(col + 8) * Gp + grp]);
+        }
+        return o;
+    };
+    Ops cur = load_ops(0);
+    Ops nx1 = load_ops(1);
     bool ok = true;
     for (int i = 0; i < nst && ok; ++i) {
         const int b = i % kStages;
@@ -232,21 +251,13 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
             else
                 issue_x(j);
         }
-        const uint4 nx2 = (i + 2 < nst) ? load_vec(i + 2) : make_uint4(0, 0, 0, 0);
+        const Ops nx2 = load_ops(i + 2);
         // weight tile b was last read by the MMAs of stage i - kStages
         if (i >= kStages && !mbar_wait(&done[b], ph ^ 1u)) ok = false;
-        if (ok) {
-            const int grp = (i * kBK) / 128;
-            int zl = 0, zh = 0;
-            __half slo = __ushort_as_half(0), shi = __ushort_as_half(0);
-            if (have_strip) {
-                zl = static_cast<int>((a.z[static_cast<size_t>(col) * zw + (grp >> 3)] >> (4 * (grp & 7))) & 0xfu) + a.zero_bias;
-                zh = static_cast<int>((a.z[static_cast<size_t>(col + 8) * zw + (grp >> 3)] >> (4 * (grp & 7))) & 0xfu) + a.zero_bias;
-                slo = a.s[static_cast<size_t>(col) * Gp + grp];
-                shi = a.s[static_cast<size_t>(col + 8) * Gp + grp];
-            }
-            dequant_store(cur, wt(b), sl * 16 + g, t, zl, zh, slo, shi);
-        }
+        if (ok)
+            dequant_store(cur.v, wt(b), sl * 16 + g, t, static_cast<int>(cur.zlo & 0xfu) + a.zero_bias,
+                          static_cast<int>(cur.zhi & 0xfu) + a.zero_bias, __ushort_as_half(cur.slo),
+                          __ushort_as_half(cur.shi));
         // make the generic-proxy stores visible to the tensor core
         fence_proxy_async_smem();
         if (ok && !mbar_wait(&full[b], ph)) ok = false;
