@@ -14,9 +14,10 @@
 //    consecutive k of two columns - to fp16 (q - zero) * scale and store them
 //    in the same 128-byte-swizzled K-major layout;
 //  * one thread issues four tcgen05.mma.kind::f16 (M=128, N=128, K=16) per
-//    64-k stage and commits them to an mbarrier; a 4-stage shared-memory ring
-//    keeps x tiles two stages ahead (TMA) and weight vectors two stages ahead
-//    (registers), so copies and dequantisation overlap the MMAs;
+//    64-k stage and commits them to an mbarrier; a 6-stage shared-memory ring
+//    keeps x tiles four stages ahead (TMA) and weight vectors, scales and
+//    zeros four stages ahead (registers), so copies and dequantisation
+//    overlap the MMAs;
 //  * the epilogue reads the accumulator with tcgen05.ld (warp w owns TMEM
 //    lanes 32w..32w+31 = rows) and writes fp16.
 // Every wait is bounded (2 s); on a timeout the block records an error bit,
@@ -39,7 +40,8 @@ constexpr int kBN = 128;         // output columns per block (MMA N)
 constexpr int kBK = 64;          // k per stage: one 128-byte swizzle row
 constexpr int kThreads = 256;
 constexpr int kTileBytes = kBM * kBK * 2;  // 16 KB (both operands)
-constexpr int kStages = 4;                 // smem ring depth (x tile + weight tile per stage)
+constexpr int kStages = 6;                 // smem ring depth (x tile + weight tile per stage)
+constexpr int kLook = 4;                   // register lookahead of weight vectors, scales, zeros
 constexpr int kSmemBytes = kStages * 2 * kTileBytes + 1024 + 256;
 
 static __device__ unsigned g_gemm_dev_error;
@@ -208,8 +210,8 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
     // x tiles run kAhead stages ahead of the MMAs: stage j goes into ring slot
     // j % kStages once the MMAs of stage j - kStages (two stages before the
     // current one) have released it, so the producer never waits on the
-    // MMAs it has just issued.  Weight vectors are prefetched two stages
-    // ahead in registers.
+    // MMAs it has just issued.  Weight vectors, scales and zeros are
+    // prefetched kLook stages ahead in registers.
     constexpr int kAhead = kStages - 2;
     auto issue_x = [&](int j) {
         const int sj = j % kStages;
@@ -237,8 +239,9 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
         }
         return o;
     };
-    Ops cur = load_ops(0);
-    Ops nx1 = load_ops(1);
+    Ops q[kLook + 1];  // q[0] = this stage, q[1..kLook] = the next ones (registers: indices are constants)
+#pragma unroll
+    for (int j = 0; j <= kLook; ++j) q[j] = load_ops(j);
     bool ok = true;
     for (int i = 0; i < nst && ok; ++i) {
         const int b = i % kStages;
@@ -251,13 +254,12 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
             else
                 issue_x(j);
         }
-        const Ops nx2 = load_ops(i + 2);
         // weight tile b was last read by the MMAs of stage i - kStages
         if (i >= kStages && !mbar_wait(&done[b], ph ^ 1u)) ok = false;
         if (ok)
-            dequant_store(cur.v, wt(b), sl * 16 + g, t, static_cast<int>(cur.zlo & 0xfu) + a.zero_bias,
-                          static_cast<int>(cur.zhi & 0xfu) + a.zero_bias, __ushort_as_half(cur.slo),
-                          __ushort_as_half(cur.shi));
+            dequant_store(q[0].v, wt(b), sl * 16 + g, t, static_cast<int>(q[0].zlo & 0xfu) + a.zero_bias,
+                          static_cast<int>(q[0].zhi & 0xfu) + a.zero_bias, __ushort_as_half(q[0].slo),
+                          __ushort_as_half(q[0].shi));
         // make the generic-proxy stores visible to the tensor core
         fence_proxy_async_smem();
         if (ok && !mbar_wait(&full[b], ph)) ok = false;
@@ -278,8 +280,9 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
             }
             mma_commit(&done[b]);
         }
-        cur = nx1;
-        nx1 = nx2;
+#pragma unroll
+        for (int j = 0; j < kLook; ++j) q[j] = q[j + 1];
+        q[kLook] = load_ops(i + kLook + 1);
     }
     // accumulator complete once the last stage's MMAs are
     bool acc_ready = false;
