@@ -371,8 +371,8 @@ def run_profile(args):
     elif args.profile == "gemm":
         _, q, z, s = synth.w4a16_inputs(1, 1024, 4096, seed=4096)
         w = mcv.pack_w4a16(q, z, s)
-        x = torch.randn((1024, 1024), device="cuda").to(torch.float16)
-        out = torch.empty((1024, 4096), dtype=torch.float16, device="cuda")
+        x = torch.randn((args.gemm_m, 1024), device="cuda").to(torch.float16)
+        out = torch.empty((args.gemm_m, 4096), dtype=torch.float16, device="cuda")
         for _ in range(5):
             mcv.matmul_w4a16_gemm(x, w, out)
     elif args.profile == "w8a8":
@@ -398,6 +398,7 @@ def main():
                     help="N>1: fused peer-mailbox exchange inside the kernel, or a separate NCCL all-reduce")
     ap.add_argument("--profile", choices=["lm_head", "w4a16", "w4a16_grouped", "w8a8", "gemm"],
                     help="run a few untimed launches of one kernel family (a small case for ncu)")
+    ap.add_argument("--gemm-m", type=int, default=1024, help="--profile gemm: activation rows M")
     ap.add_argument("--rows", type=int, default=65536, help="--profile lm_head: vocab rows (65536 = 128 MB)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

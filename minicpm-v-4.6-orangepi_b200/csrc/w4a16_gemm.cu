@@ -9,17 +9,18 @@
 // One block computes a 128 (rows of x) x 128 (output columns) tile:
 //  * x tiles [128 rows x 64 k] arrive by TMA (cp.async.bulk.tensor, 128-byte
 //    swizzle; rows past M are zero-filled by the copy engine);
-//  * the block's 256 threads dequantise the int4 weights of the tile - one
-//    16-byte lane vector of the mcv-int4 layout each, which holds 16
-//    consecutive k of two columns - to fp16 (q - zero) * scale and store them
-//    in the same 128-byte-swizzled K-major layout;
-//  * one thread issues four tcgen05.mma.kind::f16 (M=128, N=128, K=16) per
-//    64-k stage and commits them to an mbarrier; a 6-stage shared-memory ring
-//    keeps x tiles four stages ahead (TMA) and weight vectors, scales and
-//    zeros four stages ahead (registers), so copies and dequantisation
-//    overlap the MMAs;
-//  * the epilogue reads the accumulator with tcgen05.ld (warp w owns TMEM
-//    lanes 32w..32w+31 = rows) and writes fp16.
+//  * 256 dequantising threads each fetch (cp.async, five stages ahead) and
+//    dequantise one 16-byte lane vector of the mcv-int4 layout per stage -
+//    16 consecutive k of two columns - to fp16 (q - zero) * scale, store it
+//    in the same 128-byte-swizzled K-major layout and arrive on the stage's
+//    "weight ready" mbarrier;
+//  * one thread of a ninth warp requests the x tiles (four stages ahead) and
+//    issues four tcgen05.mma.kind::f16 (M=128, N=128, K=16) per 64-k stage
+//    once both operands of the stage are ready, committing them to the
+//    stage's "done" mbarrier, which frees the 5-deep tile ring slot.  The
+//    roles meet only on mbarriers: no block-wide barrier inside the k loop;
+//  * the epilogue (warps 0-3) reads the accumulator with tcgen05.ld (warp w
+//    owns TMEM lanes 32w..32w+31 = rows) and writes fp16.
 // Every wait is bounded (2 s); on a timeout the block records an error bit,
 // waits (bounded) for its own MMAs, frees its tensor memory and returns.
 // Single-GPU code: no multicast, no peer memory.
@@ -38,11 +39,13 @@ namespace {
 constexpr int kBM = 128;         // rows of x per block (MMA M)
 constexpr int kBN = 128;         // output columns per block (MMA N)
 constexpr int kBK = 64;          // k per stage: one 128-byte swizzle row
-constexpr int kThreads = 256;
+constexpr int kDqThreads = 256;  // dequantising threads: one lane vector of the tile each
+constexpr int kThreads = kDqThreads + 32;  // + one warp that issues the TMA copies and the MMAs
 constexpr int kTileBytes = kBM * kBK * 2;  // 16 KB (both operands)
-constexpr int kStages = 6;                 // smem ring depth (x tile + weight tile per stage)
-constexpr int kLook = 4;                   // register lookahead of weight vectors, scales, zeros
-constexpr int kSmemBytes = kStages * 2 * kTileBytes + 1024 + 256;
+constexpr int kStages = 5;                 // x / weight tile ring depth
+constexpr int kRawStages = 6;              // per-thread raw operand ring depth
+constexpr int kRawBytes = kDqThreads * 32; // per raw stage: each thread's int4 vector, scales, zeros
+constexpr int kSmemBytes = kStages * 2 * kTileBytes + kRawStages * kRawBytes + 1024 + 512;
 
 static __device__ unsigned g_gemm_dev_error;
 
@@ -156,16 +159,26 @@ struct GemmArgs {
     int M, K, N, zero_bias;
 };
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 __global__ void __launch_bounds__(kThreads, 1)
 w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
     extern __shared__ unsigned char smem_raw[];
     // 1024-byte alignment for the swizzle atoms
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    // x tiles, then weight tiles, one of each per ring stage
+    // x tiles and dequantised weight tiles (kStages each), then the raw ring
+    // where every dequantising thread lands its own int4 vector, scales and zeros
     auto xt = [&](int b) { return smem + b * kTileBytes; };
     auto wt = [&](int b) { return smem + (kStages + b) * kTileBytes; };
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * kStages * kTileBytes);  // [kStages]
-    uint64_t* done = full + kStages;                                                  // [kStages]
+    auto raw = [&](int b) { return smem + 2 * kStages * kTileBytes + b * kRawBytes; };
+    uint64_t* xfull = reinterpret_cast<uint64_t*>(smem + 2 * kStages * kTileBytes + kRawStages * kRawBytes);
+    uint64_t* wready = xfull + kStages;  // [kStages] weight tile dequantised (kDqThreads arrivals)
+    uint64_t* done = wready + kStages;   // [kStages] MMAs of the stage complete (tcgen05.commit)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + kStages);
     volatile int* failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -174,8 +187,9 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
     const int K = a.K, G = K / 128, Gp = (G + 7) & ~7, zw = (G + 7) >> 3;
     const int nst = K / kBK;
     const int strips_total = (a.N + 15) / 16;
+    constexpr int kIssuerWarp = kDqThreads / 32;
 
-    if (warp == 0) {
+    if (warp == kIssuerWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(kBN)
                      : "memory");
@@ -183,7 +197,8 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
     }
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
-            mbar_init(&full[i], 1);
+            mbar_init(&xfull[i], 1);
+            mbar_init(&wready[i], kDqThreads);
             mbar_init(&done[i], 1);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -193,112 +208,121 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t idesc = instr_desc_f16(kBM, kBN);
-
-    // this thread's lane vector of every stage: strip (tid / 32) of the tile
-    const int sl = tid >> 5, g = lane >> 2, t = lane & 3;
-    const int strip = (n0 >> 4) + sl;
-    const bool have_strip = strip < strips_total;
-    const int col = strip * 16 + g;
-    auto load_vec = [&](int i) -> uint4 {
-        if (!have_strip) return make_uint4(0, 0, 0, 0);
-        return ld_stream(a.qw + (static_cast<size_t>(strip) * (K / 64) + i) * 32 + lane);
-    };
 
     pdl_trigger();
     pdl_wait();  // x may be the previous kernel's output
-    // x tiles run kAhead stages ahead of the MMAs: stage j goes into ring slot
-    // j % kStages once the MMAs of stage j - kStages (two stages before the
-    // current one) have released it, so the producer never waits on the
-    // MMAs it has just issued.  Weight vectors, scales and zeros are
-    // prefetched kLook stages ahead in registers.
-    constexpr int kAhead = kStages - 2;
-    auto issue_x = [&](int j) {
-        const int sj = j % kStages;
-        mbar_expect_tx(&full[sj], kTileBytes);
-        tma_load_2d(xt(sj), &xmap, j * kBK, m0, &full[sj]);
-    };
-    if (tid == 0)
-        for (int j = 0; j < kAhead && j < nst; ++j) issue_x(j);
-    // per-stage operands of this thread: its weight vector plus the scale and
-    // zero of its two columns for the stage's 128-k group
-    struct Ops {
-        uint4 v;
-        uint32_t zlo, zhi;
-        unsigned short slo, shi;
-    };
-    auto load_ops = [&](int i) -> Ops {
-        Ops o{make_uint4(0, 0, 0, 0), 0u, 0u, 0, 0};
-        if (i < nst && have_strip) {
-            o.v = load_vec(i);
-            const int grp = (i * kBK) / 128;
-            o.zlo = a.z[static_cast<size_t>(col) * zw + (grp >> 3)] >> (4 * (grp & 7));
-            o.zhi = a.z[static_cast<size_t>(col + 8) * zw + (grp >> 3)] >> (4 * (grp & 7));
-            o.slo = __half_as_ushort(a.s[static_cast<size_t>(col) * Gp + grp]);
-            o.shi = __half_as_ushort(a.s[static_cast<size_t>(col + 8) * Gp + grp]);
-        }
-        return o;
-    };
-    Ops q[kLook + 1];  // q[0] = this stage, q[1..kLook] = the next ones (registers: indices are constants)
+
+    if (warp == kIssuerWarp) {
+        // Producer of x tiles and issuer of the MMAs.  Stage j's x tile goes
+        // into slot j % kStages once the MMAs of stage j - kStages are done;
+        // the refill for stage i + kStages - 1 is requested right after the
+        // MMAs of stage i are queued, so the tensor pipe always holds queued
+        // work while this thread waits.
+        if (lane == 0) {
+            const uint32_t idesc = instr_desc_f16(kBM, kBN);
+            auto request_x = [&](int j) {
+                const int sj = j % kStages;
+                mbar_expect_tx(&xfull[sj], kTileBytes);
+                tma_load_2d(xt(sj), &xmap, j * kBK, m0, &xfull[sj]);
+            };
+            int x_issued = 0, mma_issued = 0;
+            for (; x_issued < kStages - 1 && x_issued < nst; ++x_issued) request_x(x_issued);
+            for (int i = 0; i < nst; ++i) {
+                const int b = i % kStages;
+                const uint32_t ph = static_cast<uint32_t>(i / kStages) & 1u;
+                if (*failed || !mbar_wait(&xfull[b], ph) || !mbar_wait(&wready[b], ph)) {
+                    *failed = 1;
+                    break;
+                }
+                tc_fence_after();
 #pragma unroll
-    for (int j = 0; j <= kLook; ++j) q[j] = load_ops(j);
-    bool ok = true;
-    for (int i = 0; i < nst && ok; ++i) {
-        const int b = i % kStages;
-        const uint32_t ph = static_cast<uint32_t>(i / kStages) & 1u;
-        // refill: stage i + kAhead reuses the slot of stage i + kAhead - kStages = i - 2
-        if (tid == 0 && i + kAhead < nst) {
-            const int j = i + kAhead;
-            if (j >= kStages && !mbar_wait(&done[j % kStages], static_cast<uint32_t>((j - kStages) / kStages) & 1u))
+                for (int kk = 0; kk < kBK / 16; ++kk) {
+                    const uint64_t ad = smem_desc_sw128(smem_u32(xt(b)) + kk * 32);
+                    const uint64_t bd = smem_desc_sw128(smem_u32(wt(b)) + kk * 32);
+                    mma_f16(tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                }
+                mma_commit(&done[b]);
+                mma_issued = i + 1;
+                if (x_issued < nst) {
+                    // slot of stage x_issued = i + kStages - 1 was used by stage i - 1
+                    if (i >= 1 && !mbar_wait(&done[(i - 1) % kStages], static_cast<uint32_t>((i - 1) / kStages) & 1u)) {
+                        *failed = 1;
+                        break;
+                    }
+                    request_x(x_issued++);
+                }
+            }
+            // Drain (bounded): outstanding x copies and the issued MMAs must
+            // land before the block can free its shared and tensor memory.
+            for (int j = mma_issued; j < x_issued; ++j)
+                if (!mbar_wait(&xfull[j % kStages], static_cast<uint32_t>(j / kStages) & 1u)) *failed = 1;
+            if (mma_issued > 0 &&
+                !mbar_wait(&done[(mma_issued - 1) % kStages], static_cast<uint32_t>((mma_issued - 1) / kStages) & 1u))
                 *failed = 1;
-            else
-                issue_x(j);
+            if (mma_issued < nst) *failed = 1;
         }
-        // weight tile b was last read by the MMAs of stage i - kStages
-        if (i >= kStages && !mbar_wait(&done[b], ph ^ 1u)) ok = false;
-        if (ok)
-            dequant_store(q[0].v, wt(b), sl * 16 + g, t, static_cast<int>(q[0].zlo & 0xfu) + a.zero_bias,
-                          static_cast<int>(q[0].zhi & 0xfu) + a.zero_bias, __ushort_as_half(q[0].slo),
-                          __ushort_as_half(q[0].shi));
-        // make the generic-proxy stores visible to the tensor core
-        fence_proxy_async_smem();
-        if (ok && !mbar_wait(&full[b], ph)) ok = false;
-        if (!ok) *failed = 1;
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-        if (*failed) {
-            ok = false;
-            break;
-        }
-        if (tid == 0) {
-#pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk) {
-                const uint64_t ad = smem_desc_sw128(smem_u32(xt(b)) + kk * 32);
-                const uint64_t bd = smem_desc_sw128(smem_u32(wt(b)) + kk * 32);
-                mma_f16(tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+        __syncwarp();
+    } else {
+        // Dequantising threads: strip tid / 32 of the tile, lane vector lane.
+        // Each thread fetches its own raw operands kRawStages - 1 stages
+        // ahead (one cp.async group per stage) and reads them back itself, so
+        // the raw ring needs no barrier; the weight tile slot is reused once
+        // the MMAs of stage i - kStages are done.
+        const int sl = warp, g = lane >> 2, t = lane & 3;
+        const int strip = (n0 >> 4) + sl;
+        const bool have_strip = strip < strips_total;
+        const int col = strip * 16 + g;
+        auto request_raw = [&](int j) {
+            if (have_strip && j < nst) {
+                unsigned char* r = raw(j % kRawStages) + tid * 32;
+                const int grp = (j * kBK) / 128;
+                cp_async16(r, a.qw + (static_cast<size_t>(strip) * (K / 64) + j) * 32 + lane);
+                cp_async4(r + 16, a.s + static_cast<size_t>(col) * Gp + (grp & ~1));
+                cp_async4(r + 20, a.s + static_cast<size_t>(col + 8) * Gp + (grp & ~1));
+                cp_async4(r + 24, a.z + static_cast<size_t>(col) * zw + (grp >> 3));
+                cp_async4(r + 28, a.z + static_cast<size_t>(col + 8) * zw + (grp >> 3));
             }
-            mma_commit(&done[b]);
-        }
-#pragma unroll
-        for (int j = 0; j < kLook; ++j) q[j] = q[j + 1];
-        q[kLook] = load_ops(i + kLook + 1);
-    }
-    // accumulator complete once the last stage's MMAs are
-    bool acc_ready = false;
-    if (ok && !*failed)
-        acc_ready = mbar_wait(&done[(nst - 1) % kStages], static_cast<uint32_t>((nst - 1) / kStages) & 1u);
-    if (!acc_ready) {
-        atomicOr(&g_gemm_dev_error, kDevErrTimeout);
-        // give issued MMAs (bounded) time to finish before freeing their memory
-        if (tid == 0)
-            for (int s = 0; s < kStages && s < nst; ++s) {
-                const int last = s + ((nst - 1 - s) / kStages) * kStages;  // last stage that used slot s
-                mbar_wait(&done[s], static_cast<uint32_t>(last / kStages) & 1u);
+            cp_async_commit();  // one group per stage, empty past the end
+        };
+#pragma unroll 1
+        for (int j = 0; j < kRawStages - 1; ++j) request_raw(j);
+        for (int i = 0; i < nst; ++i) {
+            const int b = i % kStages;
+            request_raw(i + kRawStages - 1);
+            cp_async_wait<kRawStages - 1>();  // this stage's group has landed
+            if (*failed ||
+                (i >= kStages && !mbar_wait(&done[b], (static_cast<uint32_t>(i / kStages) & 1u) ^ 1u))) {
+                *failed = 1;
+                break;
             }
+            const unsigned char* r = raw(i % kRawStages) + tid * 32;
+            const int grp = (i * kBK) / 128;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            int zl = 0, zh = 0;
+            __half slo = __ushort_as_half(0), shi = __ushort_as_half(0);
+            if (have_strip) {
+                v = *reinterpret_cast<const uint4*>(r);
+                const uint32_t sp_lo = *reinterpret_cast<const uint32_t*>(r + 16);
+                const uint32_t sp_hi = *reinterpret_cast<const uint32_t*>(r + 20);
+                slo = __ushort_as_half(static_cast<unsigned short>(sp_lo >> (16 * (grp & 1))));
+                shi = __ushort_as_half(static_cast<unsigned short>(sp_hi >> (16 * (grp & 1))));
+                zl = static_cast<int>((*reinterpret_cast<const uint32_t*>(r + 24) >> (4 * (grp & 7))) & 0xfu) + a.zero_bias;
+                zh = static_cast<int>((*reinterpret_cast<const uint32_t*>(r + 28) >> (4 * (grp & 7))) & 0xfu) + a.zero_bias;
+            }
+            dequant_store(v, wt(b), sl * 16 + g, t, zl, zh, slo, shi);
+            // generic-proxy stores -> visible to the tensor core, then signal
+            fence_proxy_async_smem();
+            mbar_arrive(&wready[b]);
+        }
+        cp_async_wait<0>();
     }
+    tc_fence_before();
+    __syncthreads();
     tc_fence_after();
+    const bool acc_ready = !*failed;
+    if (!acc_ready && tid == 0) atomicOr(&g_gemm_dev_error, kDevErrTimeout);
     if (acc_ready && warp < 4) {
+        // the issuer waited for the last commit, which covers every MMA
         const int m = m0 + warp * 32 + lane;
         const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
 #pragma unroll 1
@@ -324,7 +348,8 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBN) : "memory");
+    if (warp == kIssuerWarp)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBN) : "memory");
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
@@ -366,7 +391,7 @@ int mcv_w4a16_gemm(const void* x, const void* qweight, const void* scales, const
     if (M < 1 || K < 128 || N < 1 || K % 128 != 0 || M > (1 << 24) || K > (1 << 16) || N > (1 << 24))
         return fail(MCV_ERR_SHAPE, "w4a16_gemm: need M >= 1, K a multiple of 128 (<= 65536), N >= 1");
     if (!aligned16(x) || !aligned16(qweight)) return fail(MCV_ERR_ALIGN, "w4a16_gemm: x and qweight must be 16-byte aligned");
-    if ((reinterpret_cast<uintptr_t>(scales) & 1u) || (reinterpret_cast<uintptr_t>(zeros) & 3u) ||
+    if ((reinterpret_cast<uintptr_t>(scales) & 3u) || (reinterpret_cast<uintptr_t>(zeros) & 3u) ||
         (reinterpret_cast<uintptr_t>(out) & 1u))
         return fail(MCV_ERR_ALIGN, "w4a16_gemm: misaligned scales, zeros or out");
     if (zero_bias < 0 || zero_bias > 1) return fail(MCV_ERR_VALUE, "w4a16_gemm: zero_bias must be 0 or 1");
