@@ -252,13 +252,16 @@ int mcv_lm_head_argmax_allreduce(void* comm, const void* x, const void* w, void*
                                  size_t workspace_bytes, mcv_stream_t stream);
 
 /* ---- sharded lm_head with the reduction fused into the kernel (NVLink) ---- */
-/* Each rank owns a 2 KB mailbox in its HBM and maps every peer's through
+/* Each rank owns a 1 KB mailbox in its HBM and maps every peer's through
  * CUDA IPC; the last block of each rank's lm_head kernel stores the rank's
- * argmax keys into all mailboxes (plain release stores over NVLink), waits at
- * most 1 s for the peers' keys and writes the global first-max index - one
- * kernel per rank per token, no collective launch.  All ranks must make the
- * same sequence of calls.  Set-up allocates the mailbox (cudaMalloc); calls
- * do not allocate.  Replaces the same seam as mcv_lm_head_argmax_allreduce. */
+ * argmax keys into all mailboxes (one relaxed 64-bit store per key and peer
+ * over NVLink: key and call tag share the word, so no fence is needed),
+ * waits at most 1 s for the peers' keys and writes the global first-max
+ * index - one kernel per rank per token, no collective launch.  All ranks
+ * must make the same sequence of calls.  Vocabulary indices must stay below
+ * 2^24 - 1 (n_offset + N_shard <= 16777215; MCV_ERR_SHAPE otherwise).
+ * Set-up allocates the mailbox (cudaMalloc); calls do not allocate.
+ * Replaces the same seam as mcv_lm_head_argmax_allreduce. */
 size_t mcv_p2p_handle_bytes(void);
 /* Creates this rank's context on the current device; writes its IPC handle
  * (mcv_p2p_handle_bytes() bytes) for the caller to all-gather. */

@@ -52,16 +52,20 @@ struct RowArgs {
     P2PArgs p2p;
 };
 
-__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
 __device__ __forceinline__ void st_relaxed_sys(uint64_t* p, uint64_t v) {
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
-    uint64_t v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
+// Mailbox word: bits 63..32 the key's ordered logit, bits 31..24 the call
+// tag, bits 23..0 the key's low 24 bits (0xFFFFFF - index; the host limits
+// indices below 2^24 - 1, so the key's bits 31..24 are all ones and need no
+// room).  Key 0 ("no row") is sent as logit 0 and low bits 0.
+__device__ __forceinline__ uint64_t p2p_pack(uint64_t key, uint32_t tag) {
+    const uint64_t low = key == 0 ? 0 : (key & 0xffffffull);
+    return (key & 0xffffffff00000000ull) | (static_cast<uint64_t>(tag) << 24) | low;
+}
+__device__ __forceinline__ uint64_t p2p_unpack(uint64_t word) {
+    const uint64_t hi = word & 0xffffffff00000000ull, low = word & 0xffffffull;
+    return (hi == 0 && low == 0) ? 0 : (hi | 0xff000000ull | low);
 }
 __device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t* p) {
     uint64_t v;
@@ -110,9 +114,12 @@ __device__ __noinline__ void finish_argmax(const RowArgs& a, const uint64_t (&be
             if (a.p2p.nranks > 1) {
                 // Exchange: thread j = (r, m) stores this rank's key of row m
                 // into rank r's mailbox, then waits (bounded) for rank j/M's
-                // key of row m in its own mailbox.  Slots alternate by call
-                // parity, so a fast rank's next call never overwrites a slot
-                // a slow rank has yet to read.
+                // key of row m in its own mailbox.  A slot is one 64-bit word
+                // holding the key and an 8-bit call tag (p2p_pack), so one
+                // relaxed system-scope store publishes both and no fence is
+                // needed on either side.  Slots alternate by call parity, so
+                // a fast rank's next call never overwrites a slot a slow rank
+                // has yet to read.
                 __shared__ uint64_t got[8][M];
                 __shared__ int failed;
                 if (threadIdx.x == 0) failed = 0;
@@ -120,21 +127,21 @@ __device__ __noinline__ void finish_argmax(const RowArgs& a, const uint64_t (&be
                 const int R = a.p2p.nranks;
                 const uint64_t seq = *a.p2p.seq_dev + 1;
                 const int par = static_cast<int>(seq & 1);
+                const uint32_t tag = static_cast<uint32_t>(seq & 0xffu);
                 const int j = threadIdx.x;
                 if (j < R * M) {
                     const int r = j / M, m = j % M;
-                    uint64_t* slot = a.p2p.mbox[r] + ((par * 8 + a.p2p.rank) * 8 + m) * 2;
-                    st_relaxed_sys(slot, loc[m]);
-                    st_release_sys(slot + 1, seq);
+                    st_relaxed_sys(a.p2p.mbox[r] + (par * 8 + a.p2p.rank) * 8 + m, p2p_pack(loc[m], tag));
                 }
                 if (j < R * M) {
                     const int r = j / M, m = j % M;
-                    const uint64_t* slot = a.p2p.mbox[a.p2p.rank] + ((par * 8 + r) * 8 + m) * 2;
+                    const uint64_t* slot = a.p2p.mbox[a.p2p.rank] + (par * 8 + r) * 8 + m;
                     uint64_t key = 0;
                     const uint64_t t0 = globaltimer_ns();
                     for (uint32_t spin = 0;; ++spin) {
-                        if (ld_acquire_sys(slot + 1) == seq) {
-                            key = ld_relaxed_sys(slot);
+                        const uint64_t word = ld_relaxed_sys(slot);
+                        if (((word >> 24) & 0xffu) == tag) {
+                            key = p2p_unpack(word);
                             break;
                         }
                         if ((spin & 63u) == 63u && globaltimer_ns() - t0 > 1000000000ull) {

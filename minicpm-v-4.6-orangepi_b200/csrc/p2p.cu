@@ -20,7 +20,8 @@ int lm_head_argmax_impl_p2p(const void* x, const void* w, void* out_key, void* o
 
 namespace {
 
-constexpr size_t kMboxWords = 2 * 8 * 8 * 2;               // [parity][rank][row][key, seq]
+constexpr size_t kMboxWords = 2 * 8 * 8;                   // [parity][rank][row]: key + call tag
+constexpr int64_t kP2PMaxIndex = 0xffffff;                 // indices travel in 24 bits of a mailbox word
 constexpr size_t kMboxBytes = (kMboxWords + 2) * sizeof(uint64_t);  // + call counter + error word
 
 struct P2PCtx {
@@ -108,6 +109,8 @@ int mcv_lm_head_argmax_p2p(void* ctx, const void* x, const void* w, void* out_ke
     auto* c = static_cast<P2PCtx*>(ctx);
     if (!c || !c->args.seq_dev) return fail(MCV_ERR_NULL, "lm_head_argmax_p2p: context not connected");
     if (!out_key && !out_index) return fail(MCV_ERR_NULL, "lm_head_argmax_p2p: out_key and out_index both null");
+    if (n_offset < 0 || N_shard < 0 || n_offset + N_shard > kP2PMaxIndex)
+        return fail(MCV_ERR_SHAPE, "lm_head_argmax_p2p: vocabulary indices must stay below 2^24 - 1");
     return lm_head_argmax_impl_p2p(x, w, out_key, out_index, M, K, N_shard, n_offset, fp16_logits, workspace,
                                    workspace_bytes, static_cast<cudaStream_t>(stream), &c->args);
 }

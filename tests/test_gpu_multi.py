@@ -155,6 +155,10 @@ def test_p2p_missing_peer_times_out(cuda):
         assert idx.item() == -1
         assert ctx.errors() & 1
         assert ctx.errors() == 0  # cleared by the read
+        # indices travel in 24 bits of a mailbox word: larger ones are refused
+        # on the host, before any launch
+        with pytest.raises(mcv.McvError):
+            mcv.lm_head_argmax_p2p(ctx, x, w, ws, key, idx, n_offset=(1 << 24) - 1000)
         ctx.destroy()
     finally:
         dq.put("done")
