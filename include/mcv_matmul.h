@@ -63,8 +63,16 @@ void mcv_set_pdl(int enabled);
  *   its warps (K <= 8192), 3 = streaming kernel fed by warp-private
  *   bulk-copy rings; default: K-split below 4 strips per SM, else 1.
  *   MCV_TUNE_ROWS_BLOCKS_PER_SM: blocks per SM of the persistent lm_head /
- *   [N][K] GEMV grid (1..4; default 2). */
-enum mcv_tuning_key { MCV_TUNE_W4A16_MODE = 2, MCV_TUNE_ROWS_BLOCKS_PER_SM = 3, MCV_TUNE_COUNT = 8 };
+ *   [N][K] GEMV grid (1..4; default 2).
+ *   MCV_TUNE_ROWS_PREFETCH: how many row steps ahead of its loads each warp
+ *   of that grid warms L2 (1..16; -1 = no warm-up; default: 2 when each
+ *   warp has at most 8 row steps, else none). */
+enum mcv_tuning_key {
+    MCV_TUNE_W4A16_MODE = 2,
+    MCV_TUNE_ROWS_BLOCKS_PER_SM = 3,
+    MCV_TUNE_ROWS_PREFETCH = 4,
+    MCV_TUNE_COUNT = 8
+};
 int mcv_set_tuning(int key, int value);
 /* Device-side error bits recorded since the last call (and cleared by it):
  * bit 0 = a bounded wait inside a kernel gave up (that kernel returned early
