@@ -6,21 +6,24 @@
 // (src/csrc/lib/ops.cpp:215-322) and matmul_w4a16 is M=1 only (ops.cpp:1048).
 // This kernel serves the same mcv-int4 weights as the decode GEMV.
 //
-// One block computes a 128 (rows of x) x 128 (output columns) tile:
-//  * x tiles [128 rows x 64 k] arrive by TMA (cp.async.bulk.tensor, 128-byte
-//    swizzle; rows past M are zero-filled by the copy engine);
-//  * 256 dequantising threads each fetch (cp.async, five stages ahead) and
+// One block computes a 128 (rows of x) x 256 (output columns) tile with
+// three roles that meet only on mbarriers (no block-wide barrier inside the
+// k loop):
+//  * a producer thread requests the x tiles [128 rows x 64 k] by TMA
+//    (cp.async.bulk.tensor, 128-byte swizzle; rows past M are zero-filled by
+//    the copy engine) into a 3-deep ring, refilling a slot once the MMAs that
+//    read it are done;
+//  * 512 dequantising threads each fetch (cp.async, three stages ahead) and
 //    dequantise one 16-byte lane vector of the mcv-int4 layout per stage -
 //    16 consecutive k of two columns - to fp16 (q - zero) * scale, store it
 //    in the same 128-byte-swizzled K-major layout and arrive on the stage's
 //    "weight ready" mbarrier;
-//  * one thread of a ninth warp requests the x tiles (four stages ahead) and
-//    issues four tcgen05.mma.kind::f16 (M=128, N=128, K=16) per 64-k stage
-//    once both operands of the stage are ready, committing them to the
-//    stage's "done" mbarrier, which frees the 5-deep tile ring slot.  The
-//    roles meet only on mbarriers: no block-wide barrier inside the k loop;
-//  * the epilogue (warps 0-3) reads the accumulator with tcgen05.ld (warp w
-//    owns TMEM lanes 32w..32w+31 = rows) and writes fp16.
+//  * an issuer thread runs four tcgen05.mma.kind::f16 (M=128, N=256, K=16)
+//    per 64-k stage once both operands are ready and commits them to the
+//    stage's "done" mbarrier;
+//  * the epilogue (the 16 dequantising warps) reads the accumulator with
+//    tcgen05.ld (warp w owns TMEM lanes 32(w%4).. = rows, and a quarter of
+//    the columns) and writes fp16.
 // Every wait is bounded (2 s); on a timeout the block records an error bit,
 // waits (bounded) for its own MMAs, frees its tensor memory and returns.
 // Single-GPU code: no multicast, no peer memory.
@@ -37,15 +40,18 @@ unsigned take_gemm_device_error();
 namespace {
 
 constexpr int kBM = 128;         // rows of x per block (MMA M)
-constexpr int kBN = 128;         // output columns per block (MMA N)
+constexpr int kBN = 256;         // output columns per block (MMA N)
 constexpr int kBK = 64;          // k per stage: one 128-byte swizzle row
-constexpr int kDqThreads = 256;  // dequantising threads: one lane vector of the tile each
-constexpr int kThreads = kDqThreads + 32;  // + one warp that issues the TMA copies and the MMAs
-constexpr int kTileBytes = kBM * kBK * 2;  // 16 KB (both operands)
-constexpr int kStages = 5;                 // x / weight tile ring depth
-constexpr int kRawStages = 6;              // per-thread raw operand ring depth
-constexpr int kRawBytes = kDqThreads * 32; // per raw stage: each thread's int4 vector, scales, zeros
-constexpr int kSmemBytes = kStages * 2 * kTileBytes + kRawStages * kRawBytes + 1024 + 512;
+constexpr int kStrips = kBN / 16;          // 16-column strips of the mcv-int4 layout per tile
+constexpr int kDqThreads = kBN * 2;        // dequantising threads: one lane vector of the tile each
+constexpr int kThreads = kDqThreads + 64;  // + an MMA-issuing warp and a producer warp
+constexpr int kXBytes = kBM * kBK * 2;     // 16 KB x tile per stage
+constexpr int kWBytes = kBN * kBK * 2;     // 32 KB dequantised weight tile per stage
+constexpr int kQBytes = kBN * kBK / 2;     // 8 KB packed int4 weights per stage
+constexpr int kStageBytes = kXBytes + kWBytes + kQBytes;
+constexpr int kStages = 4;                 // ring depth
+constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
 static __device__ unsigned g_gemm_dev_error;
 
@@ -166,18 +172,24 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+// Lane-uniform select of word (i & 3) of v, without dynamic register indexing.
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
+    const uint32_t lo = (i & 1) ? v.y : v.x, hi = (i & 1) ? v.w : v.z;
+    return (i & 2) ? hi : lo;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
-w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
+w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap qmap,
+                  const GemmArgs a) {
     extern __shared__ unsigned char smem_raw[];
     // 1024-byte alignment for the swizzle atoms
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    // x tiles and dequantised weight tiles (kStages each), then the raw ring
-    // where every dequantising thread lands its own int4 vector, scales and zeros
-    auto xt = [&](int b) { return smem + b * kTileBytes; };
-    auto wt = [&](int b) { return smem + (kStages + b) * kTileBytes; };
-    auto raw = [&](int b) { return smem + 2 * kStages * kTileBytes + b * kRawBytes; };
-    uint64_t* xfull = reinterpret_cast<uint64_t*>(smem + 2 * kStages * kTileBytes + kRawStages * kRawBytes);
-    uint64_t* wready = xfull + kStages;  // [kStages] weight tile dequantised (kDqThreads arrivals)
+    // per ring slot: x tile, dequantised weight tile, packed weight tile
+    auto xt = [&](int b) { return smem + b * kStageBytes; };
+    auto wt = [&](int b) { return smem + b * kStageBytes + kXBytes; };
+    auto qt = [&](int b) { return smem + b * kStageBytes + kXBytes + kWBytes; };
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);  // [kStages] x + packed tile landed
+    uint64_t* wready = full + kStages;   // [kStages] weight tile dequantised (kDqThreads arrivals)
     uint64_t* done = wready + kStages;   // [kStages] MMAs of the stage complete (tcgen05.commit)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + kStages);
     volatile int* failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -187,7 +199,7 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
     const int K = a.K, G = K / 128, Gp = (G + 7) & ~7, zw = (G + 7) >> 3;
     const int nst = K / kBK;
     const int strips_total = (a.N + 15) / 16;
-    constexpr int kIssuerWarp = kDqThreads / 32;
+    constexpr int kIssuerWarp = kDqThreads / 32, kProducerWarp = kIssuerWarp + 1;
 
     if (warp == kIssuerWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -197,7 +209,7 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
     }
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
-            mbar_init(&xfull[i], 1);
+            mbar_init(&full[i], 1);
             mbar_init(&wready[i], kDqThreads);
             mbar_init(&done[i], 1);
         }
@@ -208,29 +220,51 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-
     pdl_trigger();
-    pdl_wait();  // x may be the previous kernel's output
 
-    if (warp == kIssuerWarp) {
-        // Producer of x tiles and issuer of the MMAs.  Stage j's x tile goes
-        // into slot j % kStages once the MMAs of stage j - kStages are done;
-        // the refill for stage i + kStages - 1 is requested right after the
-        // MMAs of stage i are queued, so the tensor pipe always holds queued
-        // work while this thread waits.
+    if (warp == kProducerWarp) {
+        // Stage j's x tile and packed weight tile (16 strips x 512 B, one
+        // TMA each) go into slot j % kStages once the MMAs of stage
+        // j - kStages have released it.  The weights never depend on the
+        // previous kernel: the first slots are requested before the PDL wait.
+        if (lane == 0) {
+            auto request_q = [&](int j) {
+                const int sj = j % kStages;
+                mbar_expect_tx(&full[sj], kXBytes + kQBytes);
+                tma_load_2d(qt(sj), &qmap, j * (kQBytes / kStrips / 4), n0 / 16, &full[sj]);
+            };
+            const int pre = nst < kStages ? nst : kStages;
+            for (int j = 0; j < pre; ++j) request_q(j);
+            pdl_wait();  // x may be the previous kernel's output
+            int j = 0;
+            for (; j < nst; ++j) {
+                const int sj = j % kStages;
+                if (j >= kStages) {
+                    if (*failed || !mbar_wait(&done[sj], static_cast<uint32_t>((j - kStages) / kStages) & 1u)) {
+                        *failed = 1;
+                        break;
+                    }
+                    request_q(j);
+                }
+                tma_load_2d(xt(sj), &xmap, j * kBK, m0, &full[sj]);
+            }
+            // Drain (bounded): the newest copies of each slot must land before
+            // the block frees its shared memory; older ones were consumed.
+            const int last = j > pre ? j : pre;  // stages whose copies were requested
+            for (int q = (last > kStages ? last - kStages : 0); q < last; ++q)
+                if (!mbar_wait(&full[q % kStages], static_cast<uint32_t>(q / kStages) & 1u)) *failed = 1;
+        }
+        __syncwarp();
+    } else if (warp == kIssuerWarp) {
+        // Four tcgen05.mma (K = 16 each) per stage once its x tile has landed
+        // and its weight tile is dequantised; one commit per stage frees the slot.
         if (lane == 0) {
             const uint32_t idesc = instr_desc_f16(kBM, kBN);
-            auto request_x = [&](int j) {
-                const int sj = j % kStages;
-                mbar_expect_tx(&xfull[sj], kTileBytes);
-                tma_load_2d(xt(sj), &xmap, j * kBK, m0, &xfull[sj]);
-            };
-            int x_issued = 0, mma_issued = 0;
-            for (; x_issued < kStages - 1 && x_issued < nst; ++x_issued) request_x(x_issued);
+            int issued = 0;
             for (int i = 0; i < nst; ++i) {
                 const int b = i % kStages;
                 const uint32_t ph = static_cast<uint32_t>(i / kStages) & 1u;
-                if (*failed || !mbar_wait(&xfull[b], ph) || !mbar_wait(&wready[b], ph)) {
+                if (*failed || !mbar_wait(&full[b], ph) || !mbar_wait(&wready[b], ph)) {
                     *failed = 1;
                     break;
                 }
@@ -242,91 +276,77 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
                     mma_f16(tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
                 }
                 mma_commit(&done[b]);
-                mma_issued = i + 1;
-                if (x_issued < nst) {
-                    // slot of stage x_issued = i + kStages - 1 was used by stage i - 1
-                    if (i >= 1 && !mbar_wait(&done[(i - 1) % kStages], static_cast<uint32_t>((i - 1) / kStages) & 1u)) {
-                        *failed = 1;
-                        break;
-                    }
-                    request_x(x_issued++);
-                }
+                issued = i + 1;
             }
-            // Drain (bounded): outstanding x copies and the issued MMAs must
-            // land before the block can free its shared and tensor memory.
-            for (int j = mma_issued; j < x_issued; ++j)
-                if (!mbar_wait(&xfull[j % kStages], static_cast<uint32_t>(j / kStages) & 1u)) *failed = 1;
-            if (mma_issued > 0 &&
-                !mbar_wait(&done[(mma_issued - 1) % kStages], static_cast<uint32_t>((mma_issued - 1) / kStages) & 1u))
+            // the last commit covers every MMA issued before it
+            if (issued > 0 &&
+                !mbar_wait(&done[(issued - 1) % kStages], static_cast<uint32_t>((issued - 1) / kStages) & 1u))
                 *failed = 1;
-            if (mma_issued < nst) *failed = 1;
+            if (issued < nst) *failed = 1;
         }
         __syncwarp();
     } else {
-        // Dequantising threads: strip tid / 32 of the tile, lane vector lane.
-        // Each thread fetches its own raw operands kRawStages - 1 stages
-        // ahead (one cp.async group per stage) and reads them back itself, so
-        // the raw ring needs no barrier; the weight tile slot is reused once
-        // the MMAs of stage i - kStages are done.
+        // Dequantising threads: strip `warp` of the tile, lane vector `lane`.
+        // A landed slot implies its previous MMAs are done (the producer
+        // waited for them), so one barrier per stage suffices.  Scales and
+        // zeros of the thread's two columns come from global memory in
+        // chunks of 8 groups (one 16-byte scale vector and one zero word per
+        // column), the next chunk loaded while the current one is in use.
         const int sl = warp, g = lane >> 2, t = lane & 3;
         const int strip = (n0 >> 4) + sl;
         const bool have_strip = strip < strips_total;
         const int col = strip * 16 + g;
-        auto request_raw = [&](int j) {
-            if (have_strip && j < nst) {
-                unsigned char* r = raw(j % kRawStages) + tid * 32;
-                const int grp = (j * kBK) / 128;
-                cp_async16(r, a.qw + (static_cast<size_t>(strip) * (K / 64) + j) * 32 + lane);
-                cp_async4(r + 16, a.s + static_cast<size_t>(col) * Gp + (grp & ~1));
-                cp_async4(r + 20, a.s + static_cast<size_t>(col + 8) * Gp + (grp & ~1));
-                cp_async4(r + 24, a.z + static_cast<size_t>(col) * zw + (grp >> 3));
-                cp_async4(r + 28, a.z + static_cast<size_t>(col + 8) * zw + (grp >> 3));
+        const int nchunks = (G + 7) / 8;
+        auto load_chunk = [&](int c, uint4& slo, uint4& shi, uint32_t& zlo, uint32_t& zhi) {
+            if (have_strip && c < nchunks) {
+                slo = __ldg(reinterpret_cast<const uint4*>(a.s + static_cast<size_t>(col) * Gp) + c);
+                shi = __ldg(reinterpret_cast<const uint4*>(a.s + static_cast<size_t>(col + 8) * Gp) + c);
+                zlo = __ldg(a.z + static_cast<size_t>(col) * zw + c);
+                zhi = __ldg(a.z + static_cast<size_t>(col + 8) * zw + c);
             }
-            cp_async_commit();  // one group per stage, empty past the end
         };
-#pragma unroll 1
-        for (int j = 0; j < kRawStages - 1; ++j) request_raw(j);
+        uint4 s_lo = make_uint4(0, 0, 0, 0), s_hi = s_lo, n_lo = s_lo, n_hi = s_lo;
+        uint32_t z_lo = 0, z_hi = 0, nz_lo = 0, nz_hi = 0;
+        load_chunk(0, s_lo, s_hi, z_lo, z_hi);
+        load_chunk(1, n_lo, n_hi, nz_lo, nz_hi);
         for (int i = 0; i < nst; ++i) {
             const int b = i % kStages;
-            request_raw(i + kRawStages - 1);
-            cp_async_wait<kRawStages - 1>();  // this stage's group has landed
-            if (*failed ||
-                (i >= kStages && !mbar_wait(&done[b], (static_cast<uint32_t>(i / kStages) & 1u) ^ 1u))) {
+            const int grp = (i * kBK) / 128;
+            if (i > 0 && (grp & 7) == 0 && (i & 1) == 0) {  // first stage of a new chunk
+                s_lo = n_lo, s_hi = n_hi, z_lo = nz_lo, z_hi = nz_hi;
+                load_chunk(grp / 8 + 1, n_lo, n_hi, nz_lo, nz_hi);
+            }
+            if (*failed || !mbar_wait(&full[b], static_cast<uint32_t>(i / kStages) & 1u)) {
                 *failed = 1;
                 break;
             }
-            const unsigned char* r = raw(i % kRawStages) + tid * 32;
-            const int grp = (i * kBK) / 128;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            int zl = 0, zh = 0;
-            __half slo = __ushort_as_half(0), shi = __ushort_as_half(0);
-            if (have_strip) {
-                v = *reinterpret_cast<const uint4*>(r);
-                const uint32_t sp_lo = *reinterpret_cast<const uint32_t*>(r + 16);
-                const uint32_t sp_hi = *reinterpret_cast<const uint32_t*>(r + 20);
-                slo = __ushort_as_half(static_cast<unsigned short>(sp_lo >> (16 * (grp & 1))));
-                shi = __ushort_as_half(static_cast<unsigned short>(sp_hi >> (16 * (grp & 1))));
-                zl = static_cast<int>((*reinterpret_cast<const uint32_t*>(r + 24) >> (4 * (grp & 7))) & 0xfu) + a.zero_bias;
-                zh = static_cast<int>((*reinterpret_cast<const uint32_t*>(r + 28) >> (4 * (grp & 7))) & 0xfu) + a.zero_bias;
-            }
+            const uint4 v = *reinterpret_cast<const uint4*>(qt(b) + tid * 16);
+            const int gi = grp & 7;
+            const __half slo = __ushort_as_half(static_cast<unsigned short>(word_of(s_lo, gi >> 1) >> (16 * (gi & 1))));
+            const __half shi = __ushort_as_half(static_cast<unsigned short>(word_of(s_hi, gi >> 1) >> (16 * (gi & 1))));
+            const int zl = static_cast<int>((z_lo >> (4 * gi)) & 0xfu) + a.zero_bias;
+            const int zh = static_cast<int>((z_hi >> (4 * gi)) & 0xfu) + a.zero_bias;
             dequant_store(v, wt(b), sl * 16 + g, t, zl, zh, slo, shi);
             // generic-proxy stores -> visible to the tensor core, then signal
             fence_proxy_async_smem();
             mbar_arrive(&wready[b]);
         }
-        cp_async_wait<0>();
     }
+    if (warp != kProducerWarp) pdl_wait();  // every thread passes the wait before exit
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const bool acc_ready = !*failed;
     if (!acc_ready && tid == 0) atomicOr(&g_gemm_dev_error, kDevErrTimeout);
-    if (acc_ready && warp < 4) {
-        // the issuer waited for the last commit, which covers every MMA
-        const int m = m0 + warp * 32 + lane;
-        const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    if (acc_ready && warp < kIssuerWarp) {
+        // warp w reads TMEM lanes 32 (w % 4) .. + 31 (= rows) and its share
+        // of the columns; the issuer waited for the last commit
+        constexpr int kColsPerWarp = kBN / (kIssuerWarp / 4);
+        const int quarter = warp & 3, c0 = (warp >> 2) * kColsPerWarp;
+        const int m = m0 + quarter * 32 + lane;
+        const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
 #pragma unroll 1
-        for (int c = 0; c < kBN; c += 16) {
+        for (int c = c0; c < c0 + kColsPerWarp; c += 16) {
             float v[16];
             tmem_ld16(lane_addr + c, v);
             const int n = n0 + c;
@@ -391,28 +411,43 @@ int mcv_w4a16_gemm(const void* x, const void* qweight, const void* scales, const
     if (M < 1 || K < 128 || N < 1 || K % 128 != 0 || M > (1 << 24) || K > (1 << 16) || N > (1 << 24))
         return fail(MCV_ERR_SHAPE, "w4a16_gemm: need M >= 1, K a multiple of 128 (<= 65536), N >= 1");
     if (!aligned16(x) || !aligned16(qweight)) return fail(MCV_ERR_ALIGN, "w4a16_gemm: x and qweight must be 16-byte aligned");
-    if ((reinterpret_cast<uintptr_t>(scales) & 3u) || (reinterpret_cast<uintptr_t>(zeros) & 3u) ||
+    if ((reinterpret_cast<uintptr_t>(scales) & 15u) || (reinterpret_cast<uintptr_t>(zeros) & 3u) ||
         (reinterpret_cast<uintptr_t>(out) & 1u))
-        return fail(MCV_ERR_ALIGN, "w4a16_gemm: misaligned scales, zeros or out");
+        return fail(MCV_ERR_ALIGN, "w4a16_gemm: scales must be 16-byte, zeros 4-byte and out 2-byte aligned");
     if (zero_bias < 0 || zero_bias > 1) return fail(MCV_ERR_VALUE, "w4a16_gemm: zero_bias must be 0 or 1");
     auto enc = encode_fn();
     if (!enc) return fail(MCV_ERR_CUDA, "w4a16_gemm: cuTensorMapEncodeTiled unavailable");
-    CUtensorMap map;
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
-    const cuuint32_t box[2] = {kBK, kBM};
-    const cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(MCV_ERR_CUDA, "w4a16_gemm: cuTensorMapEncodeTiled failed");
+    CUtensorMap map, qmap;
+    {
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+        const cuuint32_t box[2] = {kBK, kBM};
+        const cuuint32_t estr[2] = {1, 1};
+        CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return fail(MCV_ERR_CUDA, "w4a16_gemm: cuTensorMapEncodeTiled(x) failed");
+    }
+    {
+        // packed weights as [strips][K/64 * 128] uint32: one 512-byte row
+        // segment per strip and 64-k stage
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K) * 2, static_cast<cuuint64_t>((N + 15) / 16)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 8};
+        const cuuint32_t box[2] = {kQBytes / kStrips / 4, kStrips};
+        const cuuint32_t estr[2] = {1, 1};
+        CUresult r = enc(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(qweight), dims, strides, box,
+                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return fail(MCV_ERR_CUDA, "w4a16_gemm: cuTensorMapEncodeTiled(qweight) failed");
+    }
     cudaError_t e = cudaFuncSetAttribute(w4a16_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a16_gemm)");
     GemmArgs ga{static_cast<const uint4*>(qweight), static_cast<const __half*>(scales),
                 static_cast<const uint32_t*>(zeros), static_cast<__half*>(out), static_cast<int>(M),
                 static_cast<int>(K), static_cast<int>(N), zero_bias};
     const dim3 grid(static_cast<unsigned>((N + kBN - 1) / kBN), static_cast<unsigned>((M + kBM - 1) / kBM));
-    return launch(w4a16_gemm_kernel, grid, dim3(kThreads), kSmemBytes, static_cast<cudaStream_t>(stream), map, ga);
+    return launch(w4a16_gemm_kernel, grid, dim3(kThreads), kSmemBytes, static_cast<cudaStream_t>(stream), map, qmap,
+                  ga);
 }
 
 }  // extern "C"
