@@ -66,11 +66,15 @@ void mcv_set_pdl(int enabled);
  *   [N][K] GEMV grid (1..4; default 2).
  *   MCV_TUNE_ROWS_PREFETCH: how many row steps ahead of its loads each warp
  *   of that grid warms L2 (1..16; -1 = no warm-up; default: 2 when each
- *   warp has at most 8 row steps, else none). */
+ *   warp has at most 8 row steps, else none).
+ *   MCV_TUNE_GEMM_SPLIT_K: k slices (1..8, thread-block cluster along z) of
+ *   mcv_w4a16_gemm; default: doubled while the output tiles times the
+ *   slices fit the SMs and every slice keeps >= 4 stages of 64 k. */
 enum mcv_tuning_key {
     MCV_TUNE_W4A16_MODE = 2,
     MCV_TUNE_ROWS_BLOCKS_PER_SM = 3,
     MCV_TUNE_ROWS_PREFETCH = 4,
+    MCV_TUNE_GEMM_SPLIT_K = 5,
     MCV_TUNE_COUNT = 8
 };
 int mcv_set_tuning(int key, int value);

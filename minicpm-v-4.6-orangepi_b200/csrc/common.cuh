@@ -50,12 +50,42 @@ int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStr
     return MCV_OK;
 }
 
+// Same, as thread-block clusters of the given shape (1x1x1: none).
+template <typename... KArgs, typename... Args>
+int launch_clustered(void (*kernel)(KArgs...), dim3 grid, dim3 block, dim3 cluster, size_t smem,
+                     cudaStream_t stream, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    unsigned n = 0;
+    if (cluster.x * cluster.y * cluster.z > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = cluster.x;
+        attr[n].val.clusterDim.y = cluster.y;
+        attr[n].val.clusterDim.z = cluster.z;
+        ++n;
+    }
+    if (pdl_enabled()) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = n;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx");
+    return MCV_OK;
+}
+
 int sm_count();
 
 // Cross-GPU exchange of the argmax keys through peer mailboxes (see
 // p2p.cu).  nranks <= 1 disables it.  Mailbox of rank r, in 64-bit words:
-// [parity 2][source rank 8][row 8][key, seq]; written by every rank over
-// NVLink with plain stores, read only by its owner.
+// [parity 2][source rank 8][row 8], one word each (key and call tag);
+// written by every rank over NVLink with plain stores, read only by its owner.
 struct P2PArgs {
     uint64_t* mbox[8];   // mailbox of each rank, as addressable from this GPU
     uint64_t* seq_dev;   // this rank's call counter (device memory)

@@ -28,6 +28,9 @@
 //    mbarrier;
 //  * the epilogue reads the accumulator (TMEM lane = weight column, column =
 //    row of x) with tcgen05.ld and writes fp16.
+// When the output tiles leave SMs idle (small M), k is split over the CTAs
+// of a thread-block cluster; the leader sums the slices' fp32 partials
+// through distributed shared memory, so no global scratch is needed.
 // Tensor memory: the accumulator (256 columns) plus a 6-deep ring of A
 // operands (32 columns per stage), 512 columns allocated per block.
 // Every wait is bounded (2 s); on a timeout the block records an error bit,
@@ -173,7 +176,30 @@ struct GemmArgs {
     __half* out;
     int M, K, N, zero_bias;
     int x_box_rows;  // rows one x tile copy lands (256, or M rounded up to 16 when smaller)
+    int splits;      // K slices = CTAs of a cluster along z (1: no split)
 };
+
+__device__ __forceinline__ uint32_t cluster_smem_addr(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ int ld_cluster_s32(uint32_t addr) {
+    int v;
+    asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
 w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap qmap,
@@ -192,7 +218,10 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n0 = blockIdx.x * kWCols, m0 = blockIdx.y * kXRows;
     const int K = a.K, G = K / 128, Gp = (G + 7) & ~7, zw = (G + 7) >> 3;
-    const int nst = K / kBK;
+    // this CTA's slice of the k stages: [i0, i0 + nst)
+    const int split = blockIdx.z;
+    const int i0 = static_cast<int>(static_cast<int64_t>(K / kBK) * split / a.splits);
+    const int nst = static_cast<int>(static_cast<int64_t>(K / kBK) * (split + 1) / a.splits) - i0;
     const int rows = a.M - m0 < kXRows ? a.M - m0 : kXRows;  // rows of x in this block
     const int mma_n = (rows + 15) & ~15;                        // MMA N: rows rounded up to 16
     const int x_bytes = a.x_box_rows * kBK * 2;
@@ -228,7 +257,7 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
             const int pre = nst < kStages ? nst : kStages;
             for (int j = 0; j < pre; ++j) {  // weights do not depend on the previous kernel
                 mbar_expect_tx(&full[j], x_bytes + kQBytes);
-                tma_load_2d(qt(j), &qmap, j * (kQBytes / kStrips / 4), n0 / 16, &full[j]);
+                tma_load_2d(qt(j), &qmap, (i0 + j) * (kQBytes / kStrips / 4), n0 / 16, &full[j]);
             }
             pdl_wait();  // x may be the previous kernel's output
             int j = 0;
@@ -240,9 +269,9 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
                         break;
                     }
                     mbar_expect_tx(&full[sj], x_bytes + kQBytes);
-                    tma_load_2d(qt(sj), &qmap, j * (kQBytes / kStrips / 4), n0 / 16, &full[sj]);
+                    tma_load_2d(qt(sj), &qmap, (i0 + j) * (kQBytes / kStrips / 4), n0 / 16, &full[sj]);
                 }
-                tma_load_2d(xt(sj), &xmap, j * kBK, m0, &full[sj]);
+                tma_load_2d(xt(sj), &xmap, (i0 + j) * kBK, m0, &full[sj]);
             }
             // Drain (bounded): every slot whose copies were fully requested
             // must land before the block frees its shared memory.
@@ -255,6 +284,9 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
         // landed and its A operand is in TMEM; one commit per stage.
         if (lane == 0) {
             const uint32_t idesc = instr_desc_f16(kWCols, mma_n);
+            // descriptor of slot 0; slot b, k-step kk adds (b * kStageBytes + 32 kk) / 16
+            // to the start-address field (no carry: shared addresses stay below 256 KB)
+            const uint64_t desc0 = smem_desc_sw128(smem_u32(xt(0)));
             int issued = 0;
             for (int i = 0; i < nst; ++i) {
                 const int b = i % kStages;
@@ -266,8 +298,9 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < kBK / 16; ++kk)
-                    mma_f16_ts(tmem_acc, tmem_a + b * kACols + kk * 8, smem_desc_sw128(smem_u32(xt(b)) + kk * 32),
-                               idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                    mma_f16_ts(tmem_acc, tmem_a + b * kACols + kk * 8,
+                               desc0 + static_cast<uint64_t>((b * kStageBytes + kk * 32) >> 4), idesc,
+                               (i > 0 || kk > 0) ? 1u : 0u);
                 mma_commit(&done[b]);
                 issued = i + 1;
             }
@@ -301,12 +334,12 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
         };
         uint4 s_cur = make_uint4(0, 0, 0, 0), s_nxt = s_cur;
         uint32_t z_cur = 0, z_nxt = 0;
-        load_chunk(0, s_cur, z_cur);
-        load_chunk(1, s_nxt, z_nxt);
+        load_chunk(i0 / 16, s_cur, z_cur);  // 16 stages of 64 k per 8-group chunk
+        load_chunk(i0 / 16 + 1, s_nxt, z_nxt);
         for (int i = 0; i < nst; ++i) {
             const int b = i % kStages;
-            const int grp = (i * kBK) / 128, gi = grp & 7;
-            if (i > 0 && (i & 15) == 0) {  // first stage of a new 8-group chunk
+            const int grp = ((i0 + i) * kBK) / 128, gi = grp & 7;
+            if (i > 0 && ((i0 + i) & 15) == 0) {  // first stage of a new 8-group chunk
                 s_cur = s_nxt, z_cur = z_nxt;
                 load_chunk(grp / 8 + 1, s_nxt, z_nxt);
             }
@@ -340,25 +373,78 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
     tc_fence_after();
     const bool acc_ready = !*failed;
     if (!acc_ready && tid == 0) atomicOr(&g_gemm_dev_error, kDevErrTimeout);
-    if (acc_ready && warp < kDqWarps) {
+    const int quarter = warp & 3;
+    const uint32_t acc_lanes = tmem_acc + (static_cast<uint32_t>(quarter * 32) << 16);
+    if (a.splits == 1) {
         // warp w reads TMEM lanes 32(w%4).. (weight columns) over columns
         // 16 j.. (rows of x) for j = w/4, w/4 + 4, ...; the issuer waited
         // for the last commit
-        const int quarter = warp & 3;
         const int col = n0 + quarter * 32 + lane;
-        const uint32_t lane_addr = tmem_acc + (static_cast<uint32_t>(quarter * 32) << 16);
+        if (acc_ready && warp < kDqWarps) {
 #pragma unroll 1
-        for (int j = warp >> 2; j * 16 < mma_n; j += kDqWarps / 4) {
-            float v[16];
-            tmem_ld16(lane_addr + j * 16, v);
-            if (col < a.N) {
+            for (int j = warp >> 2; j * 16 < mma_n; j += kDqWarps / 4) {
+                float v[16];
+                tmem_ld16(acc_lanes + j * 16, v);
+                if (col < a.N) {
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const int m = m0 + j * 16 + e;
-                    if (m < a.M) a.out[static_cast<size_t>(m) * a.N + col] = __float2half_rn(v[e]);
+                    for (int e = 0; e < 16; ++e) {
+                        const int m = m0 + j * 16 + e;
+                        if (m < a.M) a.out[static_cast<size_t>(m) * a.N + col] = __float2half_rn(v[e]);
+                    }
                 }
             }
         }
+    } else {
+        // Split k: every CTA of the cluster parks its fp32 partial sums in
+        // its own (now idle) ring memory as red[m][n]; after a cluster
+        // barrier each CTA adds all slices' partials of its share of the
+        // rows through distributed shared memory and writes fp16; a second
+        // barrier keeps every CTA's memory alive until all are done.  Every
+        // CTA reaches both barriers.
+        float* red = reinterpret_cast<float*>(smem);
+        int* red_failed = reinterpret_cast<int*>(smem + kStages * kStageBytes - 16);
+        if (warp < kDqWarps) {
+#pragma unroll 1
+            for (int j = warp >> 2; j * 16 < mma_n; j += kDqWarps / 4) {
+                float v[16];
+                tmem_ld16(acc_lanes + j * 16, v);
+#pragma unroll
+                for (int e = 0; e < 16; ++e) red[(j * 16 + e) * kWCols + quarter * 32 + lane] = v[e];
+            }
+        }
+        if (tid == 0) *red_failed = acc_ready ? 0 : 1;
+        cluster_sync();
+        // CTA `split` finishes rows m = split, split + S, ...: 32 threads per
+        // row, 4 columns each; the slices' partials are all loaded before
+        // they are added, in rank order (the same sum whichever CTA does it)
+        int any_failed = 0;
+        for (int r = 0; r < a.splits; ++r) any_failed |= ld_cluster_s32(cluster_smem_addr(red_failed, r));
+        if (!any_failed && tid < kDqThreads) {
+            const int n = 4 * (tid & 31), col = n0 + n;
+            const bool vec_ok = (a.N & 3) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 7u) == 0;
+#pragma unroll 1
+            for (int m = split + a.splits * (tid >> 5); m < rows; m += a.splits * (kDqThreads / 32)) {
+                float4 part[8];
+#pragma unroll
+                for (int r = 0; r < 8; ++r)
+                    if (r < a.splits) part[r] = ld_cluster_f32x4(cluster_smem_addr(red + m * kWCols + n, r));
+                float4 acc = part[0];
+#pragma unroll
+                for (int r = 1; r < 8; ++r)
+                    if (r < a.splits) acc.x += part[r].x, acc.y += part[r].y, acc.z += part[r].z, acc.w += part[r].w;
+                __half* o = a.out + static_cast<size_t>(m0 + m) * a.N + col;
+                if (vec_ok && col + 4 <= a.N) {
+                    *reinterpret_cast<uint2*>(o) = make_uint2(h2_as_u32(__floats2half2_rn(acc.x, acc.y)),
+                                                              h2_as_u32(__floats2half2_rn(acc.z, acc.w)));
+                } else {
+                    const float e4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        if (col + e < a.N) o[e] = __float2half_rn(e4[e]);
+                }
+            }
+        }
+        cluster_sync();
     }
     tc_fence_before();
     __syncthreads();
@@ -411,6 +497,20 @@ int mcv_w4a16_gemm(const void* x, const void* qweight, const void* scales, const
     if (zero_bias < 0 || zero_bias > 1) return fail(MCV_ERR_VALUE, "w4a16_gemm: zero_bias must be 0 or 1");
     auto enc = encode_fn();
     if (!enc) return fail(MCV_ERR_CUDA, "w4a16_gemm: cuTensorMapEncodeTiled unavailable");
+    // Split k over a cluster when the output tiles leave SMs idle: double
+    // the slices while they still fit the SMs and keep >= 4 stages each
+    // (MCV_TUNE_GEMM_SPLIT_K 1..8 overrides, limited by the stage count).
+    const int64_t tiles_n = (N + kWCols - 1) / kWCols, tiles_m = (M + kXRows - 1) / kXRows;
+    const int nst_all = static_cast<int>(K / kBK);
+    int split_k = 1;
+    const int forced = tuning(MCV_TUNE_GEMM_SPLIT_K);
+    if (forced >= 1 && forced <= 8) {
+        split_k = forced < nst_all ? forced : nst_all;
+    } else {
+        while (split_k < 8 && tiles_n * tiles_m * split_k * 2 <= sm_count() && nst_all / (split_k * 2) >= 4)
+            split_k *= 2;
+    }
+    if (tiles_m > 65535) return fail(MCV_ERR_SHAPE, "w4a16_gemm: M too large");
     // x tile box: 256 rows, or M rounded up to 16 when smaller (rows of the
     // shared-memory tile past the box keep stale values; they only feed
     // accumulator columns >= M, which are never stored)
@@ -441,11 +541,10 @@ int mcv_w4a16_gemm(const void* x, const void* qweight, const void* scales, const
     cudaError_t e = cudaFuncSetAttribute(w4a16_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a16_gemm)");
     GemmArgs ga{static_cast<const __half*>(scales), static_cast<const uint32_t*>(zeros), static_cast<__half*>(out),
-                static_cast<int>(M), static_cast<int>(K), static_cast<int>(N), zero_bias, box_rows};
-    const dim3 grid(static_cast<unsigned>((N + kWCols - 1) / kWCols),
-                    static_cast<unsigned>((M + kXRows - 1) / kXRows));
-    return launch(w4a16_gemm_kernel, grid, dim3(kThreads), kSmemBytes, static_cast<cudaStream_t>(stream), map, qmap,
-                  ga);
+                static_cast<int>(M), static_cast<int>(K), static_cast<int>(N), zero_bias, box_rows, split_k};
+    return launch_clustered(w4a16_gemm_kernel, dim3(static_cast<unsigned>(tiles_n), static_cast<unsigned>(tiles_m), split_k),
+                            dim3(kThreads), dim3(1, 1, split_k), kSmemBytes, static_cast<cudaStream_t>(stream), map,
+                            qmap, ga);
 }
 
 }  // extern "C"

@@ -139,6 +139,7 @@ def set_pdl(enabled: bool) -> None:
 TUNE_W4A16_MODE = 2
 TUNE_ROWS_BLOCKS_PER_SM = 3
 TUNE_ROWS_PREFETCH = 4
+TUNE_GEMM_SPLIT_K = 5
 
 
 def device_errors() -> int:

@@ -46,3 +46,22 @@ def test_gemm_matches_gemv_rows(cuda):
     torch.cuda.synchronize()
     assert_f16_close(g, o.cpu().numpy().astype(np.float32), what="gemm vs gemv")
     assert mcv_b200.device_errors() == 0
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 8])
+def test_gemm_split_k_cluster(cuda, splits):
+    """k split over a thread-block cluster (partials summed through
+    distributed shared memory) gives the oracle's answer for every split
+    count, including uneven slices (3) and the largest cluster (8)."""
+    import mcv_b200
+    M, K, N = 40, 2048, 640
+    x, q, z, s = synth.w4a16_inputs(M, K, N, seed=splits)
+    w = mcv_b200.pack_w4a16(q, z, s)
+    mcv_b200.set_tuning(mcv_b200.TUNE_GEMM_SPLIT_K, splits)
+    try:
+        out = run(cuda, x, w)
+    finally:
+        mcv_b200.set_tuning(mcv_b200.TUNE_GEMM_SPLIT_K, 0)
+    ref = oracle.w4a16_gemv(x, oracle.w4a16_fold_zeros(q, z), s, nthreads=8)
+    assert_f16_close(out, ref, what=f"gemm split_k={splits}")
+    assert mcv_b200.device_errors() == 0
