@@ -287,11 +287,13 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
             // descriptor of slot 0; slot b, k-step kk adds (b * kStageBytes + 32 kk) / 16
             // to the start-address field (no carry: shared addresses stay below 256 KB)
             const uint64_t desc0 = smem_desc_sw128(smem_u32(xt(0)));
-            int issued = 0;
+            int issued = 0, b = 0;
+            uint32_t ph = 0;
             for (int i = 0; i < nst; ++i) {
-                const int b = i % kStages;
-                const uint32_t ph = static_cast<uint32_t>(i / kStages) & 1u;
-                if (*failed || !mbar_wait(&full[b], ph) || !mbar_wait(&wready[b], ph)) {
+                // "weight ready" implies the slot's x tile has landed: every
+                // dequantising thread waited for the slot's full barrier
+                // (TMA completion) before arriving
+                if (*failed || !mbar_wait(&wready[b], ph)) {
                     *failed = 1;
                     break;
                 }
@@ -303,6 +305,7 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
                                (i > 0 || kk > 0) ? 1u : 0u);
                 mma_commit(&done[b]);
                 issued = i + 1;
+                if (++b == kStages) b = 0, ph ^= 1u;
             }
             // the last commit covers every MMA issued before it
             if (issued > 0 &&
