@@ -61,7 +61,7 @@ void mcv_set_pdl(int enabled);
  *   MCV_TUNE_W4A16_MODE: 1 = register-buffered streaming kernel (each warp
  *   owns whole 16-column strips), 2 = one block per strip with K split over
  *   its warps (K <= 8192), 3 = streaming kernel fed by warp-private
- *   bulk-copy rings; default: K-split below 4 strips per SM, else 1.
+ *   bulk-copy rings; default: K-split below 4 strips per SM, else 3.
  *   MCV_TUNE_ROWS_BLOCKS_PER_SM: blocks per SM of the persistent lm_head /
  *   [N][K] GEMV grid (1..4; default 2).
  *   MCV_TUNE_ROWS_PREFETCH: how many row steps ahead of its loads each warp
@@ -158,11 +158,13 @@ int mcv_w4a16_gemv(const void* x, const void* qweight, const void* scales, const
                    mcv_stream_t stream);
 
 /* out[m][n] = sum_k x[m][k] * w[k][n] for larger M (batched decode, prefill;
- * intended for M >= 16), on the tcgen05 tensor cores: x tiles by TMA, int4
- * weights dequantised to fp16 (q - zero) * scale in shared memory, fp32
- * accumulation in tensor memory, fp16 out.  Same mcv-int4 weights as
- * mcv_w4a16_gemv; group 128; x and qweight 16-byte aligned; K a multiple of
- * 128.  The reference has no quantized GEMM for M > 1: it runs prefill through
+ * intended for M >= 16), on the tcgen05 tensor cores: x and the packed int4
+ * tiles by TMA into shared memory, weights dequantised to fp16
+ * (q - zero) * scale into tensor memory as the MMA's A operand, fp32
+ * accumulation in tensor memory, fp16 out; small grids split k over a
+ * thread-block cluster (MCV_TUNE_GEMM_SPLIT_K).  Same mcv-int4 weights as
+ * mcv_w4a16_gemv; group 128; x, qweight and scales 16-byte aligned, zeros
+ * 4-byte; K a multiple of 128.  The reference has no quantized GEMM for M > 1: it runs prefill through
  * matmul_b_transposed's dense path (src/csrc/lib/ops.cpp:215-322). */
 int mcv_w4a16_gemm(const void* x, const void* qweight, const void* scales, const void* zeros,
                    int zero_bias, void* out, int64_t M, int64_t K, int64_t N, int64_t group,

@@ -260,7 +260,14 @@ w4a16_gemv_kernel(const __grid_constant__ GroupParams gp) {
 // spending registers on them, and needs no synchronisation with other warps.
 // The first kRing items are requested before griddepcontrol.wait.
 // ---------------------------------------------------------------------------
-constexpr int kRing = 2;
+#ifndef MCV_W4A16_RING
+#define MCV_W4A16_RING 2
+#endif
+constexpr int kRing = MCV_W4A16_RING;
+#ifndef MCV_W4A16_TMA_BPS
+#define MCV_W4A16_TMA_BPS 3
+#endif
+constexpr int kTmaBlocksPerSm = MCV_W4A16_TMA_BPS;
 constexpr int kStageW = 4096;                      // 8 lane vectors x 32 lanes
 constexpr int kStageBytes = kStageW + 16 * 8 + 16 * 4 + 64;  // + scales + zeros, 4352
 constexpr int kTmaSmem = kWarps * kRing * kStageBytes + kWarps * kRing * 8;
@@ -299,7 +306,7 @@ __device__ __forceinline__ void issue_item(const GroupParams& gp, const ItemIter
 }
 
 template <int M>
-__global__ void __launch_bounds__(kWarps * 32, 2)
+__global__ void __launch_bounds__(kWarps * 32, kTmaBlocksPerSm)
 w4a16_tma_kernel(const __grid_constant__ GroupParams gp) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -455,7 +462,9 @@ int launch_m(GroupParams& gp, cudaStream_t st) {
     const int strips = assign_strips(gp);
     const int mode = tuning(MCV_TUNE_W4A16_MODE);
     // few strips: one block per strip with K split over its warps; many
-    // strips: the persistent streaming kernel
+    // strips: the persistent streaming kernel fed by warp-private bulk-copy
+    // rings (3 blocks of 8 warps per SM: 0.549 vs 0.589 us per config-0 GEMV
+    // in a 48-GEMV launch against the register-buffered kernel, measured on B200)
     if (mode == 2 || (mode == 0 && strips < sm_count() * 4)) {
         int maxG = 0;
         for (int i = 0; i < gp.count; ++i) maxG = std::max(maxG, gp.p[i].K / kGroup);
@@ -467,7 +476,7 @@ int launch_m(GroupParams& gp, cudaStream_t st) {
         if (per_warp <= 8) return go(w4a16_ksplit_kernel<M, 8>);
         // larger K: the streaming kernel has no K limit
     }
-    if (mode != 3) {
+    if (mode == 1) {
         // register-buffered streaming kernel; at most kBlocksPerSm blocks per SM
         const int blocks = std::min(strips, sm_count() * kBlocksPerSm);
         return launch(w4a16_gemv_kernel<M>, dim3(blocks), dim3(kWarps * 32), 0, st, gp);
@@ -475,7 +484,7 @@ int launch_m(GroupParams& gp, cudaStream_t st) {
     auto kern = w4a16_tma_kernel<M>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTmaSmem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a16_tma)");
-    const int blocks = std::min((strips + kWarps - 1) / kWarps, sm_count() * 2);
+    const int blocks = std::min((strips + kWarps - 1) / kWarps, sm_count() * kTmaBlocksPerSm);
     return launch(kern, dim3(blocks), dim3(kWarps * 32), static_cast<size_t>(kTmaSmem), st, gp);
 }
 

@@ -174,3 +174,22 @@ def test_pack_from_tiles_rejects_wide_groups(host_pack):
     packed = oracle.w4a16_pack_tiles(w)
     with pytest.raises(RuntimeError, match="16 levels"):
         mcv_b200.pack_w4a16_from_tiles(packed, np.ones((1, N), np.float16), K, N)
+
+
+def test_tuning_keys_round_trip_and_reject_unknown():
+    """Every tuning key the header names is accepted, read back and reset to
+    its default (0); keys outside the table are refused with a status."""
+    lib = mcv_b200.lib()
+    header = open(os.path.join(ROOT, "include", "mcv_matmul.h")).read()
+    keys = {name: int(v) for name, v in re.findall(r"(MCV_TUNE_[A-Z0-9_]+) = (\d+)", header)}
+    count = keys.pop("MCV_TUNE_COUNT")
+    assert {"MCV_TUNE_W4A16_MODE", "MCV_TUNE_ROWS_BLOCKS_PER_SM", "MCV_TUNE_ROWS_PREFETCH",
+            "MCV_TUNE_GEMM_SPLIT_K"} <= set(keys)
+    for name, key in keys.items():
+        assert getattr(mcv_b200, name[len("MCV_"):]) == key
+        assert lib.mcv_set_tuning(key, 3) == 0
+        assert lib.mcv_get_tuning(key) == 3
+        assert lib.mcv_set_tuning(key, 0) == 0
+        assert lib.mcv_get_tuning(key) == 0
+    assert lib.mcv_set_tuning(count, 1) != 0
+    assert lib.mcv_set_tuning(0, 1) != 0
