@@ -330,6 +330,50 @@ int mcv_w8a8_fused(const void* x, const void* w_int8, const void* w_scale, void*
 int mcv_w8a8_quantize_weight(const void* w_kn, void* wq, void* w_scale, int64_t K, int64_t N,
                              int w_layout, mcv_stream_t stream);
 
+/* ======================================================================== */
+/* Decode dispatch: which weight format a projection's matmul runs on        */
+/* ======================================================================== */
+
+/* The MINICPM_W8A8_DECODE policy (src/csrc/lib/language_model.cpp:19-41,
+ * decoder_layer.cpp:19-25).  The mode string comes from the environment,
+ * read once per process on first use; mcv_set_w8a8_decode_mode replaces it
+ * (NULL: read the environment again on the next query).
+ *   enabled: the mode is non-empty and neither "0" nor "false";
+ *   allows(token): "all" -> every token; "1" / "selective" -> "lm_head"
+ *   only; any other mode -> the token occurs in the mode string (tokens:
+ *   mlp, linear_qkv, linear_z, linear_out, full_q, full_k, full_v, full_o,
+ *   lm_head). */
+int mcv_set_w8a8_decode_mode(const char* mode);
+int mcv_w8a8_decode_enabled(void);
+int mcv_w8a8_policy_allows(const char* token);
+/* The same rule for an explicit mode string (no process state). */
+int mcv_w8a8_policy_allows_mode(const char* mode, const char* token);
+
+/* The formats one projection has on the device; absent ones are NULL.
+ * dense: fp16, dense_layout 0 = [N][K], 1 = [K][N].  w4_*: mcv-int4
+ * (mcv_w4a16_pack_*).  w8_*: int8 [N][K] + fp16 per-channel scales
+ * (mcv_w8a8_quantize_weight with w_layout 0). */
+typedef struct mcv_decode_weights {
+    const void* dense;
+    int dense_layout;
+    const void* w4_qweight;
+    const void* w4_scales;
+    const void* w4_zeros;
+    int w4_zero_bias;
+    const void* w8_weight;
+    const void* w8_scale;
+} mcv_decode_weights;
+
+/* out fp16 [M][N] = x fp16 [M][K] . W, choosing the format like
+ * matmul_decode_dispatch (src/csrc/lib/decoder_layer.cpp:226-244): W8A8
+ * (fused quantize + int8 GEMV + dequant) when the policy is enabled, the
+ * W8A8 weight is present and M == 1; else W4A16 when present and M == 1;
+ * else the dense weight (M <= 8).  Beyond the reference: with no dense
+ * weight, M > 1 stays on the int4 weights (GEMV up to M = 8, the tcgen05
+ * GEMM above) instead of failing.  MCV_ERR_NULL when no format fits. */
+int mcv_matmul_decode_dispatch(const void* x, const mcv_decode_weights* w, void* out, int64_t M,
+                               int64_t K, int64_t N, mcv_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -70,6 +70,11 @@ _SIGS = {
     "mcv_w8a8_dequant": [_vp, _vp, _vp, _vp, _i64, _i64, _vp],
     "mcv_w8a8_fused": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
     "mcv_w8a8_quantize_weight": [_vp, _vp, _vp, _i64, _i64, _int, _vp],
+    "mcv_set_w8a8_decode_mode": [ctypes.c_char_p],
+    "mcv_w8a8_decode_enabled": [],
+    "mcv_w8a8_policy_allows": [ctypes.c_char_p],
+    "mcv_w8a8_policy_allows_mode": [ctypes.c_char_p, ctypes.c_char_p],
+    "mcv_matmul_decode_dispatch": [_vp, _vp, _vp, _i64, _i64, _i64, _vp],
 }
 _RESTYPE = {
     "mcv_status_string": ctypes.c_char_p,
@@ -416,3 +421,50 @@ def quantize_dense_weight_w8a8(w_kn, wq, w_scale, w_layout: int = 0, stream=None
     K, N = w_kn.shape
     _check(lib().mcv_w8a8_quantize_weight(_ptr(w_kn), _ptr(wq), _ptr(w_scale), K, N, w_layout, _stream(stream)),
            "quantize_dense_weight_w8a8")
+
+
+# ---- decode dispatch (matmul_decode_dispatch, decoder_layer.cpp:212-244) -------
+
+class DecodeWeights(ctypes.Structure):
+    """The formats one projection has on the device (mcv_decode_weights);
+    leave a format out by passing None."""
+    _fields_ = [("dense", _vp), ("dense_layout", _int), ("w4_qweight", _vp), ("w4_scales", _vp),
+                ("w4_zeros", _vp), ("w4_zero_bias", _int), ("w8_weight", _vp), ("w8_scale", _vp)]
+
+    @classmethod
+    def of(cls, dense=None, dense_layout: int = 0, w4: "W4A16QuantizedWeight" = None, w8=None, w8_scale=None):
+        d = cls()
+        d.dense = _ptr(dense).value if dense is not None else None
+        d.dense_layout = dense_layout
+        if w4 is not None:
+            d.w4_qweight, d.w4_scales, d.w4_zeros = (_ptr(w4.qweight).value, _ptr(w4.scales).value,
+                                                     _ptr(w4.zeros).value)
+            d.w4_zero_bias = w4.zero_bias
+        if w8 is not None:
+            d.w8_weight, d.w8_scale = _ptr(w8).value, _ptr(w8_scale).value
+        return d
+
+
+def set_w8a8_decode_mode(mode) -> None:
+    """Replace the MINICPM_W8A8_DECODE mode (None: read the environment again)."""
+    _check(lib().mcv_set_w8a8_decode_mode(None if mode is None else mode.encode()), "set_w8a8_decode_mode")
+
+
+def w8a8_decode_enabled() -> bool:
+    return bool(lib().mcv_w8a8_decode_enabled())
+
+
+def w8a8_policy_allows(token: str, mode=None) -> bool:
+    """w8a8_policy_allows (language_model.cpp:32-41); an explicit `mode`
+    bypasses the process-wide one."""
+    if mode is None:
+        return bool(lib().mcv_w8a8_policy_allows(token.encode()))
+    return bool(lib().mcv_w8a8_policy_allows_mode(mode.encode(), token.encode()))
+
+
+def matmul_decode_dispatch(x, weights: DecodeWeights, out, stream=None) -> None:
+    """out [M,N] = x [M,K] . W on the format matmul_decode_dispatch would pick."""
+    M, K = x.shape
+    N = out.shape[1]
+    _check(lib().mcv_matmul_decode_dispatch(_ptr(x), ctypes.byref(weights), _ptr(out), M, K, N, _stream(stream)),
+           "matmul_decode_dispatch")
