@@ -509,14 +509,14 @@ def main():
     s = torch.cuda.current_stream()
 
     def e2e_step(i):
-        x_dev.copy_(x_host, non_blocking=True)
         w = w_copies[i % copies]
-        if p2p is not None:
-            mcv.lm_head_argmax_p2p(p2p, x_dev, w, ws, key, idx, n_offset=a)
-        elif comm is None:
-            mcv.lm_head_argmax(x_dev, w, ws, out_index=idx)
-        else:
-            mcv.lm_head_argmax_allreduce(comm, x_dev, w, ws, key, idx, n_offset=a)
+        if comm is None:
+            # one library call: pinned x in, fused lm_head + argmax (+ peer
+            # exchange), index out, stream sync
+            mcv.lm_head_greedy_host(x_host, x_dev, w, idx, idx_host, ws, ctx=p2p, n_offset=a)
+            return
+        x_dev.copy_(x_host, non_blocking=True)
+        mcv.lm_head_argmax_allreduce(comm, x_dev, w, ws, key, idx, n_offset=a)
         idx_host.copy_(idx, non_blocking=True)
         s.synchronize()
     for i in range(3):
@@ -591,7 +591,7 @@ def main():
             "cpu_baseline": cpu_baseline,
             "e2e": {"value": round(ms_e2e * 1e3, 3), "unit": "us", "h2d_bytes_per_step": K_HIDDEN * 2,
                     "d2h_bytes_per_step": 8,
-                    "note": "pinned x H2D + C-ABI call + index D2H + stream sync per step"},
+                    "note": "one mcv_lm_head_greedy_host call per step: pinned x H2D, fused kernel, index D2H, stream sync (NCCL path: the same as separate calls)"},
             "clocks": clocks,
             "gpu_launches": args.steps * (2 if comm is not None else 1),
         }

@@ -65,6 +65,7 @@ _SIGS = {
     "mcv_p2p_destroy": [_vp],
     "mcv_p2p_errors": [_vp],
     "mcv_lm_head_argmax_p2p": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _sz, _vp],
+    "mcv_lm_head_greedy_host": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _sz, _vp],
     "mcv_w8a8_quantize": [_vp, _vp, _vp, _i64, _i64, _vp],
     "mcv_w8a8_gemm_i32": [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
     "mcv_w8a8_dequant": [_vp, _vp, _vp, _vp, _i64, _i64, _vp],
@@ -389,6 +390,21 @@ def lm_head_argmax_p2p(ctx: P2PContext, x, w_shard, workspace, out_key, out_inde
 
 
 # ---- W8A8 -----------------------------------------------------------------------
+
+def lm_head_greedy_host(x_host, x_dev, w_shard, index_dev, index_host, workspace, ctx: "P2PContext" = None,
+                        n_offset: int = 0, fp16_logits: bool = False, stream=None) -> None:
+    """Host x (pinned fp16 [M,K]) -> host int64 [M] global argmax indices in
+    one call: copy in, fused lm_head + argmax (peer exchange when `ctx`),
+    copy out, stream sync (mcv_lm_head_greedy_host)."""
+    M, K = x_host.shape
+    N = w_shard.shape[0]
+    if x_host.is_cuda or index_host.is_cuda:
+        raise RuntimeError("lm_head_greedy_host: x_host and index_host live in host memory")
+    _check(lib().mcv_lm_head_greedy_host(ctx.handle if ctx is not None else None, _vp(x_host.data_ptr()), _ptr(x_dev),
+                                         _ptr(w_shard), _ptr(index_dev), _vp(index_host.data_ptr()), M, K, N, n_offset,
+                                         int(fp16_logits), _ptr(workspace), workspace.numel(), _stream(stream)),
+           "lm_head_greedy_host")
+
 
 def w8a8_quantize(x, x_int8, x_scale, stream=None) -> None:
     M, K = x.shape

@@ -161,3 +161,26 @@ def test_argmax_last_dim(cuda):
     torch.cuda.synchronize()
     assert out.cpu().tolist() == np.argmax(logits.astype(np.float32), axis=1).tolist()
     assert out[2].item() == 77
+
+
+def test_lm_head_greedy_host_round_trip(cuda):
+    """Host x in, host index out in one call: the same index as the device
+    entry point, on two calls in a row (the workspace stays usable)."""
+    import mcv_b200 as mcv
+    torch = cuda
+    K, V = 1024, 20000
+    g = torch.Generator(device="cuda")
+    g.manual_seed(21)
+    w = (torch.randn((V, K), device="cuda", generator=g) * 0.02).half()
+    ws = mcv.lm_head_workspace(1)
+    idx_dev = torch.empty(1, dtype=torch.int64, device="cuda")
+    for seed in (1, 2):
+        x = torch.randn((1, K), generator=torch.Generator().manual_seed(seed)).half().pin_memory()
+        x_dev = torch.empty((1, K), dtype=torch.float16, device="cuda")
+        got = torch.full((1,), -7, dtype=torch.int64).pin_memory()
+        mcv.lm_head_greedy_host(x, x_dev, w, idx_dev, got, ws)
+        ref = torch.empty(1, dtype=torch.int64, device="cuda")
+        mcv.lm_head_argmax(x.cuda(), w, ws, out_index=ref)
+        torch.cuda.synchronize()
+        assert int(got[0]) == int(ref.item())
+        assert 0 <= int(got[0]) < V

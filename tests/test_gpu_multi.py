@@ -77,6 +77,15 @@ def _rank_main(rank, world, port, q):
             g.replay()
             torch.cuda.synchronize()
             seen.append(idx.cpu().tolist())
+        # one-call host path on the same context (pinned x in, index written
+        # straight into pinned host memory)
+        x_host = torch.from_numpy(x).pin_memory()
+        x_dev = torch.empty_like(xd)
+        idx_host = torch.full((M,), -7, dtype=torch.int64).pin_memory()
+        for _ in range(2):
+            idx_host.fill_(-7)
+            mcv.lm_head_greedy_host(x_host, x_dev, wd, idx, idx_host, ws, ctx=ctx, n_offset=a)
+            seen.append(idx_host.tolist())
         results["p2p"] = seen
         results["p2p_errors"] = ctx.errors()
         dist.barrier()
