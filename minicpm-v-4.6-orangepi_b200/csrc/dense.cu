@@ -20,6 +20,9 @@
 // memory, and across blocks through a 64-bit atomicMax per row and an
 // arrival counter in the caller's workspace; the last block to arrive reads
 // the result and zeroes both, so the next call needs no memset.
+#include <cstring>
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace mcv {
@@ -172,9 +175,19 @@ __device__ __noinline__ void finish_argmax(const RowArgs& a, const uint64_t (&be
         }
 }
 
+// The activation rows normally come from global memory (a.x).  A launch can
+// instead carry them in its parameters (RowArgsXP, up to kXParamChunks
+// 16-byte chunks): a host-memory x then needs no copy-in before the kernel.
+constexpr int kXParamChunks = 256;  // 4 KB: M * K <= 2048
+struct RowArgsXP {
+    RowArgs a;
+    uint4 x[kXParamChunks];
+};
+__host__ __device__ __forceinline__ const RowArgs& row_args(const RowArgs& a) { return a; }
+__host__ __device__ __forceinline__ const RowArgs& row_args(const RowArgsXP& ax) { return ax.a; }
+
 template <int M, int KCH, bool ARGMAX, bool FP16_LOGITS>
-__global__ void __launch_bounds__(kRowThreads)
-rows_kernel(RowArgs a) {
+__device__ __forceinline__ void rows_body(const RowArgs& a, const uint4* xsrc) {
     extern __shared__ uint4 xs[];  // x as [M][K/8] 16-byte chunks
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -205,7 +218,7 @@ rows_kernel(RowArgs a) {
     pdl_trigger();
     pdl_wait();
     for (int idx = threadIdx.x; idx < M * chunks; idx += kRowThreads)
-        xs[idx] = reinterpret_cast<const uint4*>(a.x)[idx];
+        xs[idx] = xsrc[idx];
     __syncthreads();
 
     uint64_t best[M];
@@ -269,6 +282,20 @@ rows_kernel(RowArgs a) {
     }
 
     if constexpr (ARGMAX) finish_argmax<M>(a, best, lane, warp);
+}
+
+template <int M, int KCH, bool ARGMAX, bool FP16_LOGITS>
+__global__ void __launch_bounds__(kRowThreads)
+rows_kernel(RowArgs a) {
+    rows_body<M, KCH, ARGMAX, FP16_LOGITS>(a, reinterpret_cast<const uint4*>(a.x));
+}
+
+// the same, with the activation rows carried in the launch parameters
+template <int M, int KCH, bool ARGMAX, bool FP16_LOGITS>
+__global__ void __launch_bounds__(kRowThreads)
+rows_kernel_xp(const __grid_constant__ RowArgsXP ax) {
+    const RowArgs a = ax.a;
+    rows_body<M, KCH, ARGMAX, FP16_LOGITS>(a, ax.x);
 }
 
 // [K][N] natural layout: each thread owns 8 consecutive columns (one 16-byte
@@ -375,29 +402,37 @@ int row_prefetch(int64_t N, int grid) {
     return (N + per_step - 1) / per_step <= 8 ? 2 : 0;
 }
 
-template <int M, bool ARGMAX, bool FP16>
-int launch_rows_m(int kch, const RowArgs& a, cudaStream_t s, int grid) {
-    const size_t smem = static_cast<size_t>(M) * a.K * 2;
+template <int M, bool ARGMAX, bool FP16, class Args>
+int launch_rows_m(int kch, const Args& args, cudaStream_t s, int grid) {
+    const size_t smem = static_cast<size_t>(M) * row_args(args).K * 2;
     auto pick = [&](auto kern) -> int {
         if (smem > 48 * 1024) {
             cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  static_cast<int>(smem));
             if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rows_kernel)");
         }
-        return launch(kern, dim3(grid), dim3(kRowThreads), smem, s, a);
+        return launch(kern, dim3(grid), dim3(kRowThreads), smem, s, args);
     };
     switch (kch) {
-        case 1: return pick(rows_kernel<M, 1, ARGMAX, FP16>);
-        case 2: return pick(rows_kernel<M, 2, ARGMAX, FP16>);
-        case 4: return pick(rows_kernel<M, 4, ARGMAX, FP16>);
-        case 8: return pick(rows_kernel<M, 8, ARGMAX, FP16>);
+        case 1:
+            if constexpr (std::is_same_v<Args, RowArgsXP>) return pick(rows_kernel_xp<M, 1, ARGMAX, FP16>);
+            else return pick(rows_kernel<M, 1, ARGMAX, FP16>);
+        case 2:
+            if constexpr (std::is_same_v<Args, RowArgsXP>) return pick(rows_kernel_xp<M, 2, ARGMAX, FP16>);
+            else return pick(rows_kernel<M, 2, ARGMAX, FP16>);
+        case 4:
+            if constexpr (std::is_same_v<Args, RowArgsXP>) return pick(rows_kernel_xp<M, 4, ARGMAX, FP16>);
+            else return pick(rows_kernel<M, 4, ARGMAX, FP16>);
+        case 8:
+            if constexpr (std::is_same_v<Args, RowArgsXP>) return pick(rows_kernel_xp<M, 8, ARGMAX, FP16>);
+            else return pick(rows_kernel<M, 8, ARGMAX, FP16>);
         default: return fail(MCV_ERR_SHAPE, "row kernel: K above 16384 unsupported");
     }
 }
 
-template <bool ARGMAX, bool FP16>
-int launch_rows(int64_t M, const RowArgs& a, cudaStream_t s, int grid) {
-    const int chunks_per_lane = (a.K / 8 + 31) / 32;
+template <bool ARGMAX, bool FP16, class Args>
+int launch_rows(int64_t M, const Args& a, cudaStream_t s, int grid) {
+    const int chunks_per_lane = (row_args(a).K / 8 + 31) / 32;
     int kch = 1;
     while (kch < chunks_per_lane) kch *= 2;
     switch (M) {
@@ -424,10 +459,13 @@ int check_rows(const void* x, const void* w, int64_t M, int64_t K, int64_t N) {
 }  // namespace
 
 // Used by the collective entry points (collective.cu, p2p.cu).
+// x_param (host memory, may be null): when set and M * K fits the launch
+// parameters, the rows are passed by value in the launch and x is not read.
 int lm_head_argmax_impl_p2p(const void* x, const void* w, void* out_key, void* out_index, int64_t M,
                             int64_t K, int64_t N, int64_t n_offset, int fp16_logits, void* ws,
-                            size_t ws_bytes, cudaStream_t s, const P2PArgs* p2p) {
-    int st = check_rows(x, w, M, K, N);
+                            size_t ws_bytes, cudaStream_t s, const P2PArgs* p2p, const void* x_param) {
+    const bool by_param = x_param != nullptr && M * K <= kXParamChunks * 8;
+    int st = check_rows(by_param ? w : x, w, M, K, N);
     if (st) return st;
     if (n_offset < 0 || n_offset + N > 0xffffffffLL) return fail(MCV_ERR_SHAPE, "lm_head: global vocab index must fit 32 bits");
     if (!ws) return fail(MCV_ERR_WORKSPACE, "lm_head: workspace is null");
@@ -446,6 +484,13 @@ int lm_head_argmax_impl_p2p(const void* x, const void* w, void* out_key, void* o
     a.K = static_cast<int>(K);
     a.n_offset = n_offset;
     if (p2p) a.p2p = *p2p;
+    if (by_param) {
+        RowArgsXP ax{};
+        ax.a = a;
+        ax.a.x = nullptr;
+        std::memcpy(ax.x, x_param, static_cast<size_t>(M * K) * 2);
+        return fp16_logits ? launch_rows<true, true>(M, ax, s, grid) : launch_rows<true, false>(M, ax, s, grid);
+    }
     return fp16_logits ? launch_rows<true, true>(M, a, s, grid) : launch_rows<true, false>(M, a, s, grid);
 }
 
@@ -463,7 +508,7 @@ int lm_head_argmax_impl(const void* x, const void* w, void* out_key, void* out_i
                         int64_t K, int64_t N, int64_t n_offset, int fp16_logits, void* ws,
                         size_t ws_bytes, cudaStream_t s) {
     return lm_head_argmax_impl_p2p(x, w, out_key, out_index, M, K, N, n_offset, fp16_logits, ws, ws_bytes, s,
-                                   nullptr);
+                                   nullptr, nullptr);
 }
 
 int key_to_index_impl(const void* key, void* out_index, int64_t M, cudaStream_t s) {

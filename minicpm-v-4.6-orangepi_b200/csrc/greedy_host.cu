@@ -1,10 +1,18 @@
 // One greedy decoding step of the lm_head from host memory to a host token
 // id in one native call: the device half of the reference's lm_head_greedy
 // (src/csrc/lib/language_model.cpp:412-482), which hands the token back to
-// the host.  Doing the copy in, the fused GEMV + argmax, the 8-byte copy out
-// and the stream synchronisation in C keeps a decode loop's per-token host
-// overhead to one library call.
+// the host.  x rides in the launch parameters when small (else one copy-in),
+// the fused GEMV + argmax stores the index straight into page-locked host
+// memory (else one 8-byte copy-out), then the stream is synchronised: one
+// library call and, for a 1024-wide row, one queued GPU operation per token.
 #include "common.cuh"
+
+namespace mcv {
+int lm_head_argmax_impl_p2p(const void* x, const void* w, void* out_key, void* out_index, int64_t M, int64_t K,
+                            int64_t N, int64_t n_offset, int fp16_logits, void* ws, size_t ws_bytes,
+                            cudaStream_t s, const P2PArgs* p2p, const void* x_param);
+const P2PArgs* p2p_args_checked(void* ctx, int64_t n_offset, int64_t N, int* status);
+}  // namespace mcv
 
 using namespace mcv;
 
@@ -16,22 +24,33 @@ int mcv_lm_head_greedy_host(void* p2p_ctx, const void* x_host, void* x_dev, cons
     if (!x_host || !x_dev || !index_dev || !index_host) return fail(MCV_ERR_NULL, "lm_head_greedy_host: null pointer");
     if (M < 1 || M > 8 || K < 1) return fail(MCV_ERR_SHAPE, "lm_head_greedy_host: M must be 1..8");
     auto s = static_cast<cudaStream_t>(stream);
-    cudaError_t e = cudaMemcpyAsync(x_dev, x_host, static_cast<size_t>(M * K) * 2, cudaMemcpyHostToDevice, s);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(x in)");
+    const P2PArgs* pa = nullptr;
+    if (p2p_ctx) {
+        int st = MCV_OK;
+        pa = p2p_args_checked(p2p_ctx, n_offset, N_shard, &st);
+        if (st) return st;
+    }
+    // Small activations (M * K <= 2048, e.g. one 1024-wide row) travel in
+    // the launch parameters: no copy-in is queued before the kernel.
+    const bool by_param = M * K <= 2048;
+    if (!by_param) {
+        cudaError_t e = cudaMemcpyAsync(x_dev, x_host, static_cast<size_t>(M * K) * 2, cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(x in)");
+    }
     // Page-locked index_host is device-addressable: the kernel's last block
     // then stores the indices straight into it and no copy-out is queued.
     void* out = index_dev;
-    cudaPointerAttributes pa{};
-    if (cudaPointerGetAttributes(&pa, index_host) == cudaSuccess && pa.type == cudaMemoryTypeHost &&
-        pa.devicePointer != nullptr)
-        out = pa.devicePointer;
+    cudaPointerAttributes pa_out{};
+    if (cudaPointerGetAttributes(&pa_out, index_host) == cudaSuccess && pa_out.type == cudaMemoryTypeHost &&
+        pa_out.devicePointer != nullptr)
+        out = pa_out.devicePointer;
     else
         (void)cudaGetLastError();  // pageable memory: not an error, copy out below
-    const int st = p2p_ctx ? mcv_lm_head_argmax_p2p(p2p_ctx, x_dev, w, nullptr, out, M, K, N_shard, n_offset,
-                                                    fp16_logits, workspace, workspace_bytes, stream)
-                           : mcv_lm_head_argmax(x_dev, w, nullptr, out, M, K, N_shard, n_offset, fp16_logits,
-                                                workspace, workspace_bytes, stream);
+    const int st = lm_head_argmax_impl_p2p(by_param ? nullptr : x_dev, w, nullptr, out, M, K, N_shard, n_offset,
+                                           fp16_logits, workspace, workspace_bytes, s, pa,
+                                           by_param ? x_host : nullptr);
     if (st) return st;
+    cudaError_t e = cudaSuccess;
     if (out == index_dev) {
         e = cudaMemcpyAsync(index_host, index_dev, static_cast<size_t>(M) * sizeof(int64_t), cudaMemcpyDeviceToHost,
                             s);

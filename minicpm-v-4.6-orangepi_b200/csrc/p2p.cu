@@ -16,7 +16,7 @@
 namespace mcv {
 int lm_head_argmax_impl_p2p(const void* x, const void* w, void* out_key, void* out_index, int64_t M, int64_t K,
                             int64_t N, int64_t n_offset, int fp16_logits, void* ws, size_t ws_bytes,
-                            cudaStream_t s, const P2PArgs* p2p);
+                            cudaStream_t s, const P2PArgs* p2p, const void* x_param);
 
 namespace {
 
@@ -32,6 +32,22 @@ struct P2PCtx {
 };
 
 }  // namespace
+// Connected context's kernel arguments for a call on rows
+// [n_offset, n_offset + N); null with *status set when the call is invalid.
+const P2PArgs* p2p_args_checked(void* ctx, int64_t n_offset, int64_t N, int* status) {
+    auto* c = static_cast<P2PCtx*>(ctx);
+    *status = MCV_OK;
+    if (!c || !c->args.seq_dev) {
+        *status = fail(MCV_ERR_NULL, "lm_head p2p: context not connected");
+        return nullptr;
+    }
+    if (n_offset < 0 || N < 0 || n_offset + N > kP2PMaxIndex) {
+        *status = fail(MCV_ERR_SHAPE, "lm_head p2p: vocabulary indices must stay below 2^24 - 1");
+        return nullptr;
+    }
+    return &c->args;
+}
+
 }  // namespace mcv
 
 using namespace mcv;
@@ -112,7 +128,7 @@ int mcv_lm_head_argmax_p2p(void* ctx, const void* x, const void* w, void* out_ke
     if (n_offset < 0 || N_shard < 0 || n_offset + N_shard > kP2PMaxIndex)
         return fail(MCV_ERR_SHAPE, "lm_head_argmax_p2p: vocabulary indices must stay below 2^24 - 1");
     return lm_head_argmax_impl_p2p(x, w, out_key, out_index, M, K, N_shard, n_offset, fp16_logits, workspace,
-                                   workspace_bytes, static_cast<cudaStream_t>(stream), &c->args);
+                                   workspace_bytes, static_cast<cudaStream_t>(stream), &c->args, nullptr);
 }
 
 }  // extern "C"
