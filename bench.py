@@ -508,12 +508,15 @@ def main():
     e2e_steps = min(args.steps, 100)
     s = torch.cuda.current_stream()
 
+    greedy = None if comm is not None else mcv.LmHeadGreedyStep(x_host, x_dev, w_copies[0], idx, idx_host, ws,
+                                                                 ctx=p2p, n_offset=a, stream=s)
+
     def e2e_step(i):
         w = w_copies[i % copies]
-        if comm is None:
-            # one library call: pinned x in, fused lm_head + argmax (+ peer
-            # exchange), index out, stream sync
-            mcv.lm_head_greedy_host(x_host, x_dev, w, idx, idx_host, ws, ctx=p2p, n_offset=a)
+        if greedy is not None:
+            # one library call: x in the launch, fused lm_head + argmax (+ peer
+            # exchange), index into pinned memory, stream sync
+            greedy(w)
             return
         x_dev.copy_(x_host, non_blocking=True)
         mcv.lm_head_argmax_allreduce(comm, x_dev, w, ws, key, idx, n_offset=a)

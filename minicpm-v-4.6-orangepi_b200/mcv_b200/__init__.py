@@ -406,6 +406,34 @@ def lm_head_greedy_host(x_host, x_dev, w_shard, index_dev, index_host, workspace
            "lm_head_greedy_host")
 
 
+class LmHeadGreedyStep:
+    """A prepared mcv_lm_head_greedy_host call for a decode loop: tensors are
+    checked and their addresses resolved once, so each token costs one
+    library call (pass `w_shard` to switch weights between calls)."""
+
+    def __init__(self, x_host, x_dev, w_shard, index_dev, index_host, workspace, ctx: "P2PContext" = None,
+                 n_offset: int = 0, fp16_logits: bool = False, stream=None):
+        if x_host.is_cuda or index_host.is_cuda:
+            raise RuntimeError("LmHeadGreedyStep: x_host and index_host live in host memory")
+        M, K = x_host.shape
+        self._fn = lib().mcv_lm_head_greedy_host
+        self._shape = (M, K)
+        self._rows = w_shard.shape[0]
+        self._head = (ctx.handle if ctx is not None else None, _vp(x_host.data_ptr()), _ptr(x_dev))
+        self._w = _ptr(w_shard)
+        self._tail = (_ptr(index_dev), _vp(index_host.data_ptr()), M, K)
+        self._rest = (n_offset, int(fp16_logits), _ptr(workspace), workspace.numel(), _stream(stream))
+        self._keep = (x_host, x_dev, w_shard, index_dev, index_host, workspace)
+
+    def __call__(self, w_shard=None) -> None:
+        w = self._w
+        if w_shard is not None:
+            if tuple(w_shard.shape) != (self._rows, self._shape[1]):
+                raise RuntimeError("LmHeadGreedyStep: weight shape differs from the prepared one")
+            w = _ptr(w_shard)
+        _check(self._fn(*self._head, w, *self._tail, self._rows, *self._rest), "lm_head_greedy_host")
+
+
 def w8a8_quantize(x, x_int8, x_scale, stream=None) -> None:
     M, K = x.shape
     _check(lib().mcv_w8a8_quantize(_ptr(x), _ptr(x_int8), _ptr(x_scale), M, K, _stream(stream)), "w8a8_quantize")

@@ -184,3 +184,25 @@ def test_lm_head_greedy_host_round_trip(cuda):
         torch.cuda.synchronize()
         assert int(got[0]) == int(ref.item())
         assert 0 <= int(got[0]) < V
+
+
+def test_lm_head_greedy_step_prepared(cuda):
+    """The prepared per-token call gives the same indices as the plain call,
+    also after switching the weight between calls."""
+    import mcv_b200 as mcv
+    torch = cuda
+    K, V = 1024, 12000
+    g = torch.Generator(device="cuda")
+    g.manual_seed(22)
+    ws_ = [(torch.randn((V, K), device="cuda", generator=g) * 0.02).half() for _ in range(2)]
+    work = mcv.lm_head_workspace(1)
+    idx_dev = torch.empty(1, dtype=torch.int64, device="cuda")
+    x = torch.randn((1, K), generator=torch.Generator().manual_seed(5)).half().pin_memory()
+    x_dev = torch.empty((1, K), dtype=torch.float16, device="cuda")
+    got = torch.full((1,), -7, dtype=torch.int64).pin_memory()
+    step = mcv.LmHeadGreedyStep(x, x_dev, ws_[0], idx_dev, got, work)
+    for w in (ws_[0], ws_[1], ws_[0]):
+        step(w)
+        ref = torch.full((1,), -9, dtype=torch.int64).pin_memory()
+        mcv.lm_head_greedy_host(x, x_dev, w, idx_dev, ref, work)
+        assert int(got[0]) == int(ref[0]) and 0 <= int(got[0]) < V
