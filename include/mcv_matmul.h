@@ -292,14 +292,16 @@ int mcv_lm_head_argmax_p2p(void* ctx, const void* x, const void* w, void* out_ke
 
 /* One greedy step from host memory to a host token id, as the reference's
  * lm_head_greedy hands the token back (src/csrc/lib/language_model.cpp:412-482;
- * its rms_norm stays with the caller): copies x (M rows, fp16, from host
- * memory - pinned for an asynchronous copy) to x_dev, runs
- * mcv_lm_head_argmax (p2p_ctx NULL) or mcv_lm_head_argmax_p2p (p2p_ctx from
- * mcv_p2p_create/connect) on this rank's rows, hands the M int64 global
- * indices to index_host and synchronises the stream.  When index_host is
- * page-locked the kernel stores the indices into it directly; otherwise
- * they go through index_dev (M int64 on the device) and a copy.
- * Synchronous; same workspace rules as mcv_lm_head_argmax. */
+ * its rms_norm stays with the caller): runs mcv_lm_head_argmax (p2p_ctx
+ * NULL) or mcv_lm_head_argmax_p2p (p2p_ctx from mcv_p2p_create/connect) on
+ * this rank's rows for x (M rows, fp16, in host memory), hands the M int64
+ * global indices to index_host and synchronises the stream.  x travels in
+ * the kernel's launch parameters when M * K <= 2048 (read during this call);
+ * larger x is copied to x_dev first (pin x_host for an asynchronous copy).
+ * When index_host is page-locked the kernel stores the indices into it
+ * directly; otherwise they go through index_dev (M int64 on the device) and a
+ * copy.  x_dev and index_dev are required either way.  Synchronous; same
+ * workspace rules as mcv_lm_head_argmax. */
 int mcv_lm_head_greedy_host(void* p2p_ctx, const void* x_host, void* x_dev, const void* w, void* index_dev,
                             int64_t* index_host, int64_t M, int64_t K, int64_t N_shard, int64_t n_offset,
                             int fp16_logits, void* workspace, size_t workspace_bytes, mcv_stream_t stream);
