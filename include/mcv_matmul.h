@@ -69,12 +69,16 @@ void mcv_set_pdl(int enabled);
  *   warp has at most 8 row steps, else none).
  *   MCV_TUNE_GEMM_SPLIT_K: k slices (1..8, thread-block cluster along z) of
  *   mcv_w4a16_gemm; default: doubled while the output tiles times the
- *   slices fit the SMs and every slice keeps >= 4 stages of 64 k. */
+ *   slices fit the SMs and every slice keeps >= 4 stages of 64 k.
+ *   MCV_TUNE_W8A8_KERNEL: the [N][K] W8A8 kernel - 1 = DP4A dot products,
+ *   2 = integer tensor-core MMAs (mma.sync m16n8k32 s8); default: DP4A for
+ *   M = 1, MMAs from M = 2.  Both give the same bits. */
 enum mcv_tuning_key {
     MCV_TUNE_W4A16_MODE = 2,
     MCV_TUNE_ROWS_BLOCKS_PER_SM = 3,
     MCV_TUNE_ROWS_PREFETCH = 4,
     MCV_TUNE_GEMM_SPLIT_K = 5,
+    MCV_TUNE_W8A8_KERNEL = 6,
     MCV_TUNE_COUNT = 8
 };
 int mcv_set_tuning(int key, int value);

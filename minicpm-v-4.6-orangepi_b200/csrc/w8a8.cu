@@ -85,6 +85,87 @@ struct W8Args {
     int N;
 };
 
+// Fused prologue: quantizes the M activation rows of a.x (fp16 [M][K]) into
+// xq8 (int8, row stride `stride` bytes) and their fp16-rounded scales into
+// xscale_s, per row exactly as w8a8_quantize; block 0 also writes the
+// optional copies.  VPT = 16-byte x vectors per thread per row.
+template <int M, int VPT>
+__device__ __forceinline__ void fused_quantize_x(const W8Args& a, int8_t* xq8, int stride, float* xscale_s) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // All M rows are loaded into registers with independent 16-byte loads
+    // (one L2 round trip), reduced to per-row maxima, then quantized from
+    // the same registers into shared memory.
+    constexpr int T = kW8Warps * 32;
+    const uint4* xh4 = static_cast<const uint4*>(a.x);
+    const int vpr = a.K >> 3;  // 16-byte vectors per row
+    uint4 xr[M][VPT];
+    float mx[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+#pragma unroll
+        for (int t = 0; t < VPT; ++t) {
+            const int v = threadIdx.x + t * T;
+            xr[m][t] = v < vpr ? xh4[m * vpr + v] : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+        mx[m] = 0.0f;
+#pragma unroll
+        for (int t = 0; t < VPT; ++t) {
+            const uint32_t wd[4] = {xr[m][t].x, xr[m][t].y, xr[m][t].z, xr[m][t].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = __half22float2(u32_as_h2(wd[e]));
+                mx[m] = fmaxf(mx[m], fmaxf(fabsf(f.x), fabsf(f.y)));
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], o));
+    __shared__ float red_m[kW8Warps][M];
+    __shared__ float inv_s[M];
+    if (lane == 0) {
+#pragma unroll
+        for (int m = 0; m < M; ++m) red_m[warp][m] = mx[m];
+    }
+    __syncthreads();
+    if (threadIdx.x < M) {
+        const int m = threadIdx.x;
+        float r = 0.0f;
+        for (int i = 0; i < kW8Warps; ++i) r = fmaxf(r, red_m[i][m]);
+        const float scale = scale_from_absmax(r);
+        inv_s[m] = __fdiv_rn(1.0f, scale);
+        const __half sh = __float2half_rn(scale);
+        xscale_s[m] = __half2float(sh);
+        if (blockIdx.x == 0 && a.xs_out) a.xs_out[m] = sh;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+        const float inv = inv_s[m];
+#pragma unroll
+        for (int t = 0; t < VPT; ++t) {
+            const int v = threadIdx.x + t * T;
+            if (v >= vpr) continue;
+            const uint32_t wd[4] = {xr[m][t].x, xr[m][t].y, xr[m][t].z, xr[m][t].w};
+            uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = __half22float2(u32_as_h2(wd[e]));
+                const uint32_t q0 = static_cast<uint8_t>(quant_act(f.x, inv));
+                const uint32_t q1 = static_cast<uint8_t>(quant_act(f.y, inv));
+                packed[e >> 1] |= (q0 | (q1 << 8)) << (16 * (e & 1));
+            }
+            *reinterpret_cast<uint2*>(xq8 + m * stride + v * 8) = make_uint2(packed[0], packed[1]);
+            if (blockIdx.x == 0 && a.xq_out)
+                *reinterpret_cast<uint2*>(a.xq_out + static_cast<int64_t>(m) * a.K + v * 8) =
+                    make_uint2(packed[0], packed[1]);
+        }
+    }
+}
+
 template <int M, int KCH, bool FUSED>
 __global__ void __launch_bounds__(kW8Warps * 32)
 w8_rows_kernel(W8Args a) {
@@ -116,79 +197,7 @@ w8_rows_kernel(W8Args a) {
 
     int8_t* xq8 = reinterpret_cast<int8_t*>(xq_s);
     if constexpr (FUSED) {
-        // All M rows are loaded into registers with independent 16-byte loads
-        // (one L2 round trip), reduced to per-row maxima, then quantized from
-        // the same registers into shared memory.
-        constexpr int T = kW8Warps * 32;
-        constexpr int VPT = (KCH + 3) / 4;  // 16-byte x vectors per thread per row (K <= 512*KCH)
-        const uint4* xh4 = static_cast<const uint4*>(a.x);
-        const int vpr = a.K >> 3;  // 16-byte vectors per row
-        uint4 xr[M][VPT];
-        float mx[M];
-#pragma unroll
-        for (int m = 0; m < M; ++m)
-#pragma unroll
-            for (int t = 0; t < VPT; ++t) {
-                const int v = threadIdx.x + t * T;
-                xr[m][t] = v < vpr ? xh4[m * vpr + v] : make_uint4(0, 0, 0, 0);
-            }
-#pragma unroll
-        for (int m = 0; m < M; ++m) {
-            mx[m] = 0.0f;
-#pragma unroll
-            for (int t = 0; t < VPT; ++t) {
-                const uint32_t wd[4] = {xr[m][t].x, xr[m][t].y, xr[m][t].z, xr[m][t].w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = __half22float2(u32_as_h2(wd[e]));
-                    mx[m] = fmaxf(mx[m], fmaxf(fabsf(f.x), fabsf(f.y)));
-                }
-            }
-        }
-#pragma unroll
-        for (int m = 0; m < M; ++m)
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], o));
-        __shared__ float red_m[kW8Warps][M];
-        __shared__ float inv_s[M];
-        if (lane == 0) {
-#pragma unroll
-            for (int m = 0; m < M; ++m) red_m[warp][m] = mx[m];
-        }
-        __syncthreads();
-        if (threadIdx.x < M) {
-            const int m = threadIdx.x;
-            float r = 0.0f;
-            for (int i = 0; i < kW8Warps; ++i) r = fmaxf(r, red_m[i][m]);
-            const float scale = scale_from_absmax(r);
-            inv_s[m] = __fdiv_rn(1.0f, scale);
-            const __half sh = __float2half_rn(scale);
-            xscale_s[m] = __half2float(sh);
-            if (blockIdx.x == 0 && a.xs_out) a.xs_out[m] = sh;
-        }
-        __syncthreads();
-#pragma unroll
-        for (int m = 0; m < M; ++m) {
-            const float inv = inv_s[m];
-#pragma unroll
-            for (int t = 0; t < VPT; ++t) {
-                const int v = threadIdx.x + t * T;
-                if (v >= vpr) continue;
-                const uint32_t wd[4] = {xr[m][t].x, xr[m][t].y, xr[m][t].z, xr[m][t].w};
-                uint32_t packed[2] = {0u, 0u};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = __half22float2(u32_as_h2(wd[e]));
-                    const uint32_t q0 = static_cast<uint8_t>(quant_act(f.x, inv));
-                    const uint32_t q1 = static_cast<uint8_t>(quant_act(f.y, inv));
-                    packed[e >> 1] |= (q0 | (q1 << 8)) << (16 * (e & 1));
-                }
-                *reinterpret_cast<uint2*>(xq8 + m * a.K + v * 8) = make_uint2(packed[0], packed[1]);
-                if (blockIdx.x == 0 && a.xq_out)
-                    *reinterpret_cast<uint2*>(a.xq_out + static_cast<int64_t>(m) * a.K + v * 8) =
-                        make_uint2(packed[0], packed[1]);
-            }
-        }
+        fused_quantize_x<M, (KCH + 3) / 4>(a, xq8, a.K, xscale_s);
     } else {
         const uint4* src = static_cast<const uint4*>(a.x);
         for (int idx = threadIdx.x; idx < M * chunks; idx += kW8Warps * 32) xq_s[idx] = src[idx];
@@ -236,6 +245,108 @@ w8_rows_kernel(W8Args a) {
                 }
             }
         }
+}
+
+// ---- int8 GEMV over [N][K] weights on the integer tensor cores ----------------
+// mma.sync m16n8k32 s8 x s8 -> s32: a block owns 16 weight rows (the MMA's M)
+// and its 8 warps split K in 64-k blocks.  Lane (g = lane/4, t = lane%4)
+// loads 16 bytes of rows g and g+8 at k = 64 kb + 16 t; k is permuted
+// identically for weights and activations inside each 64-k block (an integer
+// dot product does not depend on the order of k), so those bytes are directly
+// the A fragments of two MMAs and one 16-byte shared-memory load of x row g is
+// the matching B fragments.  The activation rows are the MMA's N (M <= 8).
+// int32 sums are exact in any order: the cross-warp sum in shared memory and
+// the dequant epilogue give the DP4A kernel's bits.
+constexpr int kXqPad = 16;  // bytes between x rows in shared memory (bank spread)
+
+__device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <int M, int KB, bool FUSED>
+__global__ void __launch_bounds__(kW8Warps * 32)
+w8_mma_kernel(W8Args a) {
+    extern __shared__ uint4 xq_s[];  // int8 x, M rows of K + kXqPad bytes
+    __shared__ float xscale_s[M];
+    __shared__ int4 red[kW8Warps][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int n0 = blockIdx.x * 16;
+    const int K = a.K, nkb = (K + 63) / 64, stride = K + kXqPad;
+    const bool lo_ok = n0 + g < a.N, hi_ok = n0 + g + 8 < a.N;
+
+    // this warp's weight bytes of rows g and g+8 (all before the PDL wait)
+    uint4 wlo[KB], whi[KB];
+#pragma unroll
+    for (int j = 0; j < KB; ++j) {
+        const int kb = warp + j * kW8Warps;
+        const int k = kb * 64 + 16 * t;
+        wlo[j] = whi[j] = make_uint4(0, 0, 0, 0);
+        if (kb < nkb && k < K) {
+            if (lo_ok) wlo[j] = ld_stream(a.w + static_cast<int64_t>(n0 + g) * K + k);
+            if (hi_ok) whi[j] = ld_stream(a.w + static_cast<int64_t>(n0 + g + 8) * K + k);
+        }
+    }
+    float wsc_lo = 0.0f, wsc_hi = 0.0f;
+    if constexpr (FUSED) {
+        if (lo_ok) wsc_lo = __half2float(a.w_scale[n0 + g]);
+        if (hi_ok) wsc_hi = __half2float(a.w_scale[n0 + g + 8]);
+    }
+    pdl_trigger();
+    pdl_wait();
+
+    int8_t* xq8 = reinterpret_cast<int8_t*>(xq_s);
+    if constexpr (FUSED) {
+        fused_quantize_x<M, (KB + 3) / 4>(a, xq8, stride, xscale_s);
+    } else {
+        const uint4* src = static_cast<const uint4*>(a.x);
+        const int cpr = K >> 4;  // 16-byte chunks per row
+        for (int idx = threadIdx.x; idx < M * cpr; idx += kW8Warps * 32) {
+            const int m = idx / cpr, c = idx - m * cpr;
+            *reinterpret_cast<uint4*>(xq8 + m * stride + c * 16) = src[idx];
+        }
+    }
+    __syncthreads();
+
+    int d[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < KB; ++j) {
+        const int kb = warp + j * kW8Warps;
+        const int k = kb * 64 + 16 * t;
+        if (kb >= nkb) break;
+        uint4 xv = make_uint4(0, 0, 0, 0);
+        if (g < M && k < K) xv = *reinterpret_cast<const uint4*>(xq8 + g * stride + k);
+        mma_s8(d, wlo[j].x, whi[j].x, wlo[j].y, whi[j].y, xv.x, xv.y);
+        mma_s8(d, wlo[j].z, whi[j].z, wlo[j].w, whi[j].w, xv.z, xv.w);
+    }
+    red[warp][lane] = make_int4(d[0], d[1], d[2], d[3]);
+    __syncthreads();
+    if (warp == 0) {
+        int4 sum = red[0][lane];
+#pragma unroll
+        for (int w = 1; w < kW8Warps; ++w) {
+            const int4 r = red[w][lane];
+            sum.x += r.x, sum.y += r.y, sum.z += r.z, sum.w += r.w;
+        }
+        // D rows g / g+8 = weight rows n0+g / n0+g+8, columns 2t / 2t+1 = activation rows
+        const int vals[4] = {sum.x, sum.y, sum.z, sum.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int m = 2 * t + (e & 1);
+            const int n = n0 + g + 8 * (e >> 1);
+            if (m >= M || n >= a.N) continue;
+            const int64_t o = static_cast<int64_t>(m) * a.N + n;
+            if (a.acc) a.acc[o] = vals[e];
+            if constexpr (FUSED) {
+                const float wsc = (e >> 1) ? wsc_hi : wsc_lo;
+                a.out[o] = __float2half_rn(__fmul_rn(__fmul_rn(__int2float_rn(vals[e]), wsc), xscale_s[m]));
+            }
+        }
+    }
 }
 
 // ---- int8 GEMV over the reference's [K][N] weights --------------------------------
@@ -376,7 +487,32 @@ __global__ void quantize_weight_kernel(const __half* __restrict__ w, int8_t* __r
 }
 
 template <int M, bool FUSED>
+int launch_w8_mma_m(const W8Args& a, cudaStream_t s) {
+    const int nkb = (a.K + 63) / 64;
+    const int per_warp = (nkb + kW8Warps - 1) / kW8Warps;
+    const dim3 grid((a.N + 15) / 16);
+    const dim3 block(kW8Warps * 32);
+    const size_t smem = static_cast<size_t>(M) * (a.K + kXqPad);
+    auto go = [&](auto kern) -> int {
+        if (smem > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w8_mma)");
+        }
+        return launch(kern, grid, block, smem, s, a);
+    };
+    if (per_warp <= 1) return go(w8_mma_kernel<M, 1, FUSED>);
+    if (per_warp <= 2) return go(w8_mma_kernel<M, 2, FUSED>);
+    if (per_warp <= 4) return go(w8_mma_kernel<M, 4, FUSED>);
+    if (per_warp <= 8) return go(w8_mma_kernel<M, 8, FUSED>);
+    return fail(MCV_ERR_SHAPE, "w8a8: K above 4096 unsupported on the [N][K] path");
+}
+
+template <int M, bool FUSED>
 int launch_w8_rows_m(const W8Args& a, cudaStream_t s) {
+    // one activation row: DP4A is quicker (1.93 vs 2.18 us at N=3584); from
+    // four rows the tensor cores are (2.73 vs 4.05 us at M=4, N=3584), B200
+    const int t = tuning(MCV_TUNE_W8A8_KERNEL);
+    if (t == 2 || (t != 1 && M >= 2)) return launch_w8_mma_m<M, FUSED>(a, s);
     const int chunks_per_lane = (a.K / 16 + 31) / 32;
     int kch = 1;
     while (kch < chunks_per_lane) kch *= 2;

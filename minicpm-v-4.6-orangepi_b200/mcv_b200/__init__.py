@@ -146,6 +146,7 @@ TUNE_W4A16_MODE = 2
 TUNE_ROWS_BLOCKS_PER_SM = 3
 TUNE_ROWS_PREFETCH = 4
 TUNE_GEMM_SPLIT_K = 5
+TUNE_W8A8_KERNEL = 6
 
 
 def device_errors() -> int:

@@ -130,3 +130,31 @@ def test_quantize_weight_exact(cuda, layout):
     got = H(wq) if layout == 1 else H(wq).T
     assert np.array_equal(got, rq)
     assert np.array_equal(H(sc), rs)
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 8])
+def test_dp4a_and_tensor_core_kernels_same_bits(cuda, M):
+    """The DP4A and the mma.sync s8 kernels give the same int32 sums and the
+    same fp16 outputs (integer sums are exact in any order)."""
+    import mcv_b200 as mcv
+    torch = cuda
+    K, N = 2048, 520
+    x, w8, ws8 = synth.w8a8_inputs(M, K, N, seed=40 + M)
+    xd = torch.from_numpy(x).cuda()
+    wt = torch.from_numpy(np.ascontiguousarray(w8.T)).cuda()
+    wsd = torch.from_numpy(ws8).cuda()
+    got = {}
+    for kern in (1, 2):
+        mcv.set_tuning(mcv.TUNE_W8A8_KERNEL, kern)
+        try:
+            out = torch.empty((M, N), dtype=torch.float16, device="cuda")
+            acc = torch.empty((M, N), dtype=torch.int32, device="cuda")
+            mcv.w8a8_fused(xd, wt, wsd, out, acc=acc, w_layout=0)
+            torch.cuda.synchronize()
+            got[kern] = (out.cpu().numpy().view(np.uint16), acc.cpu().numpy())
+        finally:
+            mcv.set_tuning(mcv.TUNE_W8A8_KERNEL, 0)
+    assert np.array_equal(got[1][1], got[2][1])
+    assert np.array_equal(got[1][0], got[2][0])
+    _, r8 = oracle.w8a8_fused(x, w8, ws8)
+    assert np.array_equal(got[2][0], r8)
