@@ -23,6 +23,15 @@ int mcv_lm_head_greedy_host(void* p2p_ctx, const void* x_host, void* x_dev, cons
                             int fp16_logits, void* workspace, size_t workspace_bytes, mcv_stream_t stream) {
     if (!x_host || !x_dev || !index_dev || !index_host) return fail(MCV_ERR_NULL, "lm_head_greedy_host: null pointer");
     if (M < 1 || M > 8 || K < 1) return fail(MCV_ERR_SHAPE, "lm_head_greedy_host: M must be 1..8");
+    // x_host is read on the host when it travels in the launch: refuse
+    // device memory rather than fault the process
+    cudaPointerAttributes pa_in{};
+    if (cudaPointerGetAttributes(&pa_in, x_host) == cudaSuccess) {
+        if (pa_in.type == cudaMemoryTypeDevice)
+            return fail(MCV_ERR_VALUE, "lm_head_greedy_host: x_host must be host memory");
+    } else {
+        (void)cudaGetLastError();  // unregistered host memory
+    }
     auto s = static_cast<cudaStream_t>(stream);
     const P2PArgs* pa = nullptr;
     if (p2p_ctx) {

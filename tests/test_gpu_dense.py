@@ -206,3 +206,22 @@ def test_lm_head_greedy_step_prepared(cuda):
         ref = torch.full((1,), -9, dtype=torch.int64).pin_memory()
         mcv.lm_head_greedy_host(x, x_dev, w, idx_dev, ref, work)
         assert int(got[0]) == int(ref[0]) and 0 <= int(got[0]) < V
+
+
+def test_lm_head_greedy_host_refuses_device_x(cuda):
+    """x_host is read on the host: device memory there is refused with a
+    status instead of faulting the process."""
+    import ctypes
+    import mcv_b200 as mcv
+    torch = cuda
+    L = mcv.lib()
+    xd = torch.zeros((1, 1024), dtype=torch.float16, device="cuda")
+    w = torch.zeros((64, 1024), dtype=torch.float16, device="cuda")
+    ws = mcv.lm_head_workspace(1)
+    idx = torch.empty(1, dtype=torch.int64, device="cuda")
+    host_idx = torch.empty(1, dtype=torch.int64).pin_memory()
+    st = L.mcv_lm_head_greedy_host(None, ctypes.c_void_p(xd.data_ptr()), ctypes.c_void_p(xd.data_ptr()),
+                                   ctypes.c_void_p(w.data_ptr()), ctypes.c_void_p(idx.data_ptr()),
+                                   ctypes.c_void_p(host_idx.data_ptr()), 1, 1024, 64, 0, 0,
+                                   ctypes.c_void_p(ws.data_ptr()), ws.numel(), None)
+    assert st == 7 and b"host memory" in L.mcv_last_error()
