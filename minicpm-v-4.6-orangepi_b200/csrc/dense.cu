@@ -19,7 +19,13 @@
 // reduction is an integer max: per warp in registers, per block in shared
 // memory, and across blocks through a 64-bit atomicMax per row and an
 // arrival counter in the caller's workspace; the last block to arrive reads
-// the result and zeroes both, so the next call needs no memset.
+// the result and zeroes both, so the next call needs no memset.  Each warp
+// warms L2 a tunable number of row steps ahead of its loads
+// (cp.async.bulk.prefetch.L2), and the first rows are loaded before
+// griddepcontrol.wait.  A second launch form carries the activation rows in
+// the kernel parameters (rows_kernel_xp) for callers whose x is in host
+// memory; with a peer-exchange context the last block also runs the
+// cross-GPU exchange (see finish_argmax).
 #include <cstring>
 #include <type_traits>
 

@@ -14,12 +14,19 @@
 //    feeds to one m16n8k16 tensor-core MMA as its A fragment (rows = the 16
 //    columns of the strip).  So one coalesced 16-byte load per lane brings the
 //    fragments of four MMAs, and a warp-wide load reads 512 contiguous bytes.
-//  * Work.  A persistent grid; each warp owns whole strips (all of K) and
-//    walks them in chunks of 512 k: the next chunk's eight 16-byte loads per
-//    lane are issued before the current chunk is computed (register double
-//    buffering, ~64 KB per SM in flight).  The first chunk is loaded before
-//    griddepcontrol.wait, so under programmatic dependent launch the weight
-//    stream overlaps the previous kernel.
+//  * Work.  Three schedules (MCV_TUNE_W4A16_MODE picks one explicitly):
+//    - K-split (default for a launch with few strips, i.e. one decode GEMV):
+//      one block per strip, its 8 warps take the strip's 128-k groups and
+//      meet in shared memory - one load latency on the critical path;
+//    - bulk-copy streaming (default for large launches): a persistent grid,
+//      each warp owns whole strips and walks them in 512-k chunks that land
+//      in a warp-private 2-deep cp.async.bulk ring while the previous chunk
+//      is computed (3 blocks of 8 warps per SM);
+//    - register streaming: the same walk with the next chunk's eight 16-byte
+//      loads per lane held in registers (2 blocks per SM).
+//    Weights are requested before griddepcontrol.wait in all three, so under
+//    programmatic dependent launch the weight stream overlaps the previous
+//    kernel.
 //  * Math.  int4 -> fp16 by the exponent-bias ("magic number") conversion
 //    described for FasterTransformer-style mixed-input GEMMs (Kim et al.,
 //    "Who Says Elephants Can't Run", 2022; Frantar et al., MARLIN, 2024):
