@@ -278,6 +278,36 @@ def bench_w4a16_gemm(torch, mcv, synth, l2, hbm, tflops):
     return {"config": "config4 W4A16 GEMM, tcgen05.mma kind::f16, fp32 accumulation in TMEM, K=1024", "cases": res}
 
 
+def bench_lm_head_w8a8(torch, mcv, hbm, lm_w):
+    """The W8A8 branch of lm_head_greedy: the embedding quantized per row to
+    int8 (254 MB, above 2x L2 on its own), fused int8 GEMV + dequant + argmax
+    per token, CUDA graph of 20 back-to-back tokens."""
+    V, K = lm_w.shape
+    wq = torch.empty((V, K), dtype=torch.int8, device="cuda")
+    wsc = torch.empty(V, dtype=torch.float16, device="cuda")
+    mcv.quantize_dense_weight_w8a8(lm_w, wq, wsc, w_layout=2)
+    x = torch.randn((1, K), device="cuda").to(torch.float16)
+    work = mcv.lm_head_workspace(1)
+    idx = torch.empty(1, dtype=torch.int64, device="cuda")
+    steps = 20
+
+    def run():
+        for _ in range(steps):
+            mcv.lm_head_argmax_w8a8(x, wq, wsc, work, out_index=idx)
+    run()
+    torch.cuda.synchronize()
+    g = graph_of(torch, run, torch.cuda.Stream())
+    g.replay()
+    torch.cuda.synchronize()
+    us = time_graph_ms(torch, g, reps=5) / steps * 1e3
+    byts = V * K + V * 2 + K * 2
+    gbs = byts / (us * 1e-6) / 1e9
+    del g
+    return {"config": "config1 vocabulary, W8A8 lm_head + argmax (int8 rows, per-row scales), M=1",
+            "us_per_token": round(us, 3), "bytes_per_token": byts, "GBps": round(gbs, 1),
+            "frac_of_hbm": round(gbs / hbm, 4)}
+
+
 def bench_decode_step(torch, mcv, synth, hbm, lm_w, ws_lm):
     """Config 3: the 186 projections of one token + the lm_head.  'separate'
     launches each projection on its own (the reference's call pattern);
@@ -569,6 +599,7 @@ def main():
             extras["w8a8"] = bench_w8a8(torch, mcv, synth, l2, hbm)
             extras["decode_step"] = bench_decode_step(torch, mcv, synth, hbm, w_copies[0], ws)
             extras["w4a16_gemm"] = bench_w4a16_gemm(torch, mcv, synth, l2, hbm, _tf)
+            extras["lm_head_w8a8"] = bench_lm_head_w8a8(torch, mcv, hbm, w_copies[0])
 
     if rank == 0:
         algo_bytes = rows * K_HIDDEN * 2 + K_HIDDEN * 2 + 8

@@ -343,9 +343,25 @@ int mcv_w8a8_fused(const void* x, const void* w_int8, const void* w_scale, void*
                    void* acc_out, void* x_int8_out, void* x_scale_out, int64_t M, int64_t K,
                    int64_t N, int w_layout, mcv_stream_t stream);
 
-/* Per-output-channel int8 quantization of an fp16 weight stored [K][N]:
- * w_scale fp16 [N] (truncating fp16 conversion, as the reference), wq int8 in
- * w_layout 0 ([N][K]) or 1 ([K][N]).
+/* Fused W8A8 lm_head + greedy argmax: the W8A8 branch of lm_head_greedy
+ * (src/csrc/lib/language_model.cpp:430-479, taken when MINICPM_W8A8_DECODE
+ * allows "lm_head").  x fp16 [M][K] is quantized per row in the kernel (as
+ * mcv_w8a8_quantize); w_int8 holds int8 weight rows [N_shard][K] with fp16
+ * per-row scales w_scale (mcv_w8a8_quantize_weight with w_layout 2 from the
+ * fp16 embedding); each logit is RN((acc * w_scale) * x_scale) to fp16, read
+ * with subnormals as zero like the reference's host argmax, and the first
+ * maximum's global index (n_offset + row) is returned.  K a multiple of 16,
+ * at most 4096; M = 1..8; workspace as mcv_lm_head_argmax; out_key uses the
+ * same order-preserving format (shards combine by max, e.g. through
+ * mcv_argmax_key_to_index after an all-reduce). */
+int mcv_lm_head_argmax_w8a8(const void* x, const void* w_int8, const void* w_scale, void* out_key,
+                            void* out_index, int64_t M, int64_t K, int64_t N_shard, int64_t n_offset,
+                            void* workspace, size_t workspace_bytes, mcv_stream_t stream);
+
+/* Per-output-channel int8 quantization of an fp16 weight: w_scale fp16 [N]
+ * (truncating fp16 conversion, as the reference).  w_layout 0: input [K][N],
+ * wq [N][K]; 1: input [K][N], wq [K][N]; 2: input [N][K] (e.g. the tied
+ * embedding for mcv_lm_head_argmax_w8a8), wq [N][K].
  * Replaces quantize_dense_weight_w8a8 (src/csrc/lib/quantized_weight.cpp:231-268). */
 int mcv_w8a8_quantize_weight(const void* w_kn, void* wq, void* w_scale, int64_t K, int64_t N,
                              int w_layout, mcv_stream_t stream);

@@ -30,6 +30,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "w8a8_quant.cuh"
 
 namespace mcv {
 namespace {
@@ -59,6 +60,7 @@ struct RowArgs {
     int prefetch;           // L2 warm-up distance in row steps (0: none)
     int64_t n_offset;
     P2PArgs p2p;
+    const __half* w_scale;  // int8 lm_head: per-row weight scales [N] (w then holds int8 rows)
 };
 
 __device__ __forceinline__ void st_relaxed_sys(uint64_t* p, uint64_t v) {
@@ -453,6 +455,161 @@ int launch_rows(int64_t M, const Args& a, cudaStream_t s, int grid) {
     }
 }
 
+// ---- int8 (W8A8) lm_head + greedy argmax ------------------------------------
+// The W8A8 branch of lm_head_greedy (src/csrc/lib/language_model.cpp:430-479):
+// x is quantized per row as w8a8_quantize does, each logit is the int32 dot
+// with a weight row dequantized as w8a8_dequant does, RN((acc * ws) * xs) to
+// fp16, and the host reads those fp16 logits with subnormals flushed to zero
+// (its h2f, :444-458) before the strict '>' first-max scan.  Same walk as
+// rows_body over int8 rows of K bytes (half the fp16 traffic), same keys and
+// last-block finish (peer exchange included).
+
+// fp16 -> float the way the reference's host argmax reads logits
+__device__ __forceinline__ float h2f_flush_subnormal(__half h) {
+    const unsigned short b = __half_as_ushort(h);
+    if (((b >> 10) & 0x1fu) == 0u) return (b & 0x8000u) ? -0.0f : 0.0f;
+    return __half2float(h);
+}
+
+template <int M, int KCH>
+__global__ void __launch_bounds__(kRowThreads)
+rows_w8_kernel(RowArgs a) {
+    extern __shared__ uint4 xs[];  // int8 x as [M][K/16] 16-byte chunks
+    __shared__ float xscale_s[M];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int chunks = a.K >> 4;
+    const int64_t gwarp = static_cast<int64_t>(blockIdx.x) * kRowWarps + warp;
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kRowWarps;
+    const uint4* w4 = reinterpret_cast<const uint4*>(a.w);
+
+    uint4 wv[kRowsPerStep][KCH];
+    float wsc[kRowsPerStep];
+    int64_t r = gwarp * kRowsPerStep;
+    const int64_t step = nwarps * kRowsPerStep;
+#pragma unroll
+    for (int t = 0; t < kRowsPerStep; ++t) {
+        wsc[t] = r + t < a.N ? __half2float(a.w_scale[r + t]) : 0.0f;
+#pragma unroll
+        for (int i = 0; i < KCH; ++i) {
+            const int c = lane + 32 * i;
+            wv[t][i] = make_uint4(0, 0, 0, 0);
+            if (r + t < a.N && c < chunks) wv[t][i] = ld_stream(w4 + (r + t) * chunks + c);
+        }
+    }
+    if (lane < kRowsPerStep * a.prefetch) {
+        const int64_t pr = r + step * (1 + lane / kRowsPerStep) + (lane % kRowsPerStep);
+        if (pr < a.N) prefetch_l2(w4 + pr * chunks, static_cast<uint32_t>(a.K));
+    }
+    pdl_trigger();
+    pdl_wait();
+    quantize_rows_to_smem<M, (KCH + 3) / 4, kRowThreads>(a.x, a.K, reinterpret_cast<int8_t*>(xs), a.K, xscale_s,
+                                                         nullptr, nullptr);
+    __syncthreads();
+
+    uint64_t best[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) best[m] = 0;
+
+    while (r < a.N) {
+        int acc[kRowsPerStep][M];
+#pragma unroll
+        for (int t = 0; t < kRowsPerStep; ++t)
+#pragma unroll
+            for (int m = 0; m < M; ++m) acc[t][m] = 0;
+#pragma unroll
+        for (int i = 0; i < KCH; ++i) {
+            const int c = lane + 32 * i;
+            if (c < chunks) {
+#pragma unroll
+                for (int m = 0; m < M; ++m) {
+                    const uint4 xv = xs[m * chunks + c];
+#pragma unroll
+                    for (int t = 0; t < kRowsPerStep; ++t) {
+                        int v = acc[t][m];
+                        v = __dp4a(static_cast<int>(wv[t][i].x), static_cast<int>(xv.x), v);
+                        v = __dp4a(static_cast<int>(wv[t][i].y), static_cast<int>(xv.y), v);
+                        v = __dp4a(static_cast<int>(wv[t][i].z), static_cast<int>(xv.z), v);
+                        v = __dp4a(static_cast<int>(wv[t][i].w), static_cast<int>(xv.w), v);
+                        acc[t][m] = v;
+                    }
+                }
+            }
+        }
+        // issue the next step's loads before reducing this one
+        const int64_t rn = r + step;
+        if (lane < kRowsPerStep && a.prefetch > 0) {
+            const int64_t pr = rn + step * a.prefetch + lane;
+            if (pr < a.N) prefetch_l2(w4 + pr * chunks, static_cast<uint32_t>(a.K));
+        }
+        float wsn[kRowsPerStep];
+#pragma unroll
+        for (int t = 0; t < kRowsPerStep; ++t) {
+            wsn[t] = rn + t < a.N ? __half2float(a.w_scale[rn + t]) : 0.0f;
+#pragma unroll
+            for (int i = 0; i < KCH; ++i) {
+                const int c = lane + 32 * i;
+                if (rn + t < a.N && c < chunks) wv[t][i] = ld_stream(w4 + (rn + t) * chunks + c);
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < kRowsPerStep; ++t) {
+            const int64_t row = r + t;
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                int v = acc[t][m];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (row < a.N) {
+                    const __half h = __float2half_rn(__fmul_rn(__fmul_rn(__int2float_rn(v), wsc[t]), xscale_s[m]));
+                    const uint64_t key = argmax_key(h2f_flush_subnormal(h), static_cast<uint32_t>(a.n_offset + row));
+                    best[m] = key > best[m] ? key : best[m];
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < kRowsPerStep; ++t) wsc[t] = wsn[t];
+        r = rn;
+    }
+    finish_argmax<M>(a, best, lane, warp);
+}
+
+template <int M>
+int launch_rows_w8_m(int kch, const RowArgs& a, cudaStream_t s, int grid) {
+    const size_t smem = static_cast<size_t>(M) * a.K;
+    auto pick = [&](auto kern) -> int {
+        if (smem > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(smem));
+            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rows_w8_kernel)");
+        }
+        return launch(kern, dim3(grid), dim3(kRowThreads), smem, s, a);
+    };
+    switch (kch) {
+        case 1: return pick(rows_w8_kernel<M, 1>);
+        case 2: return pick(rows_w8_kernel<M, 2>);
+        case 4: return pick(rows_w8_kernel<M, 4>);
+        case 8: return pick(rows_w8_kernel<M, 8>);
+        default: return fail(MCV_ERR_SHAPE, "lm_head_w8a8: K above 4096 unsupported");
+    }
+}
+
+int launch_rows_w8(int64_t M, const RowArgs& a, cudaStream_t s, int grid) {
+    const int chunks_per_lane = (a.K / 16 + 31) / 32;
+    int kch = 1;
+    while (kch < chunks_per_lane) kch *= 2;
+    switch (M) {
+        case 1: return launch_rows_w8_m<1>(kch, a, s, grid);
+        case 2: return launch_rows_w8_m<2>(kch, a, s, grid);
+        case 3: return launch_rows_w8_m<3>(kch, a, s, grid);
+        case 4: return launch_rows_w8_m<4>(kch, a, s, grid);
+        case 5: return launch_rows_w8_m<5>(kch, a, s, grid);
+        case 6: return launch_rows_w8_m<6>(kch, a, s, grid);
+        case 7: return launch_rows_w8_m<7>(kch, a, s, grid);
+        default: return launch_rows_w8_m<8>(kch, a, s, grid);
+    }
+}
+
 int check_rows(const void* x, const void* w, int64_t M, int64_t K, int64_t N) {
     if (!x || !w) return fail(MCV_ERR_NULL, "null x or w");
     if (M < 1 || M > 8) return fail(MCV_ERR_SHAPE, "M must be 1..8");
@@ -498,6 +655,42 @@ int lm_head_argmax_impl_p2p(const void* x, const void* w, void* out_key, void* o
         return fp16_logits ? launch_rows<true, true>(M, ax, s, grid) : launch_rows<true, false>(M, ax, s, grid);
     }
     return fp16_logits ? launch_rows<true, true>(M, a, s, grid) : launch_rows<true, false>(M, a, s, grid);
+}
+
+// W8A8 lm_head: int8 weight rows [N][K] + fp16 per-row scales (see rows_w8_kernel).
+int lm_head_argmax_w8a8_impl(const void* x, const void* w, const void* w_scale, void* out_key, void* out_index,
+                             int64_t M, int64_t K, int64_t N, int64_t n_offset, void* ws, size_t ws_bytes,
+                             cudaStream_t s, const P2PArgs* p2p) {
+    if (!w_scale) return fail(MCV_ERR_NULL, "lm_head_w8a8: null weight scales");
+    int st = check_rows(x, w, M, K, N);
+    if (st) return st;
+    if (K % 16 != 0 || K > 4096) return fail(MCV_ERR_SHAPE, "lm_head_w8a8: K must be a multiple of 16, at most 4096");
+    if (n_offset < 0 || n_offset + N > 0xffffffffLL) return fail(MCV_ERR_SHAPE, "lm_head: global vocab index must fit 32 bits");
+    if (!ws) return fail(MCV_ERR_WORKSPACE, "lm_head: workspace is null");
+    if (ws_bytes < mcv_lm_head_workspace_size(M)) return fail(MCV_ERR_WORKSPACE, "lm_head: workspace too small");
+    if (reinterpret_cast<uintptr_t>(ws) & 7u) return fail(MCV_ERR_ALIGN, "lm_head: workspace must be 8-byte aligned");
+    // int8 rows are half as long as fp16 ones: 4 blocks per SM (48
+    // registers) keep as many bytes in flight as the fp16 kernel's 2
+    // (MCV_TUNE_ROWS_BLOCKS_PER_SM overrides)
+    const int t = tuning(MCV_TUNE_ROWS_BLOCKS_PER_SM);
+    const int64_t warps_needed = (N + kRowsPerStep - 1) / kRowsPerStep;
+    const int64_t blocks_needed = (warps_needed + kRowWarps - 1) / kRowWarps;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * ((t >= 1 && t <= 4) ? t : 4);
+    const int grid = static_cast<int>(blocks_needed < cap ? blocks_needed : cap);
+    RowArgs a{};
+    a.prefetch = row_prefetch(N, grid);
+    a.x = static_cast<const __half*>(x);
+    a.w = static_cast<const __half*>(w);
+    a.w_scale = static_cast<const __half*>(w_scale);
+    a.counter = static_cast<unsigned*>(ws);
+    a.keys = reinterpret_cast<uint64_t*>(static_cast<char*>(ws) + 64);
+    a.out_key = static_cast<uint64_t*>(out_key);
+    a.out_index = static_cast<int64_t*>(out_index);
+    a.N = N;
+    a.K = static_cast<int>(K);
+    a.n_offset = n_offset;
+    if (p2p) a.p2p = *p2p;
+    return launch_rows_w8(M, a, s, grid);
 }
 
 unsigned take_dense_device_error() {
@@ -600,6 +793,15 @@ int mcv_argmax_key_to_index(const void* key, void* out_index, int64_t M, mcv_str
     if (!key || !out_index) return fail(MCV_ERR_NULL, "argmax_key_to_index: null pointer");
     if (M < 1 || M > 32) return fail(MCV_ERR_SHAPE, "argmax_key_to_index: M must be 1..32");
     return key_to_index_impl(key, out_index, M, static_cast<cudaStream_t>(stream));
+}
+
+
+int mcv_lm_head_argmax_w8a8(const void* x, const void* w_int8, const void* w_scale, void* out_key, void* out_index,
+                            int64_t M, int64_t K, int64_t N_shard, int64_t n_offset, void* workspace,
+                            size_t workspace_bytes, mcv_stream_t stream) {
+    if (!out_key && !out_index) return fail(MCV_ERR_NULL, "lm_head_argmax_w8a8: out_key and out_index both null");
+    return lm_head_argmax_w8a8_impl(x, w_int8, w_scale, out_key, out_index, M, K, N_shard, n_offset, workspace,
+                                    workspace_bytes, static_cast<cudaStream_t>(stream), nullptr);
 }
 
 }  // extern "C"

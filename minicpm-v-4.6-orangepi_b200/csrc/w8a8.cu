@@ -21,6 +21,7 @@
 // kernel quantizes x inside every block (x is a few KB in L2), prefetches its
 // weights before the PDL wait, and writes fp16 outputs directly.
 #include "common.cuh"
+#include "w8a8_quant.cuh"
 
 namespace mcv {
 namespace {
@@ -28,19 +29,6 @@ namespace {
 constexpr int kQThreads = 256;
 constexpr int kW8Warps = 8;
 constexpr int kW8Cpw = 2;
-
-__device__ __forceinline__ int8_t quant_act(float v, float inv) {
-    float q = __fmul_rn(v, inv);
-    q = q > 127.0f ? 127.0f : q;
-    q = q < -128.0f ? -128.0f : q;
-    q = q >= 0.0f ? __fadd_rn(q, 0.5f) : __fsub_rn(q, 0.5f);
-    return static_cast<int8_t>(__float2int_rz(q));
-}
-
-__device__ __forceinline__ float scale_from_absmax(float max_abs) {
-    float s = __fdiv_rn(max_abs, 127.0f);
-    return s < 0.00000001f ? 0.00000001f : s;
-}
 
 // Block-wide max of non-negative floats (bit pattern order == value order).
 __device__ __forceinline__ float block_max_nonneg(float v, float* red) {
@@ -85,85 +73,13 @@ struct W8Args {
     int N;
 };
 
-// Fused prologue: quantizes the M activation rows of a.x (fp16 [M][K]) into
-// xq8 (int8, row stride `stride` bytes) and their fp16-rounded scales into
-// xscale_s, per row exactly as w8a8_quantize; block 0 also writes the
-// optional copies.  VPT = 16-byte x vectors per thread per row.
+// Fused prologue: quantizes the M activation rows of a.x into xq8 (row
+// stride `stride` bytes) and their fp16-rounded scales into xscale_s, per
+// row exactly as w8a8_quantize; block 0 also writes the optional copies.
 template <int M, int VPT>
 __device__ __forceinline__ void fused_quantize_x(const W8Args& a, int8_t* xq8, int stride, float* xscale_s) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    // All M rows are loaded into registers with independent 16-byte loads
-    // (one L2 round trip), reduced to per-row maxima, then quantized from
-    // the same registers into shared memory.
-    constexpr int T = kW8Warps * 32;
-    const uint4* xh4 = static_cast<const uint4*>(a.x);
-    const int vpr = a.K >> 3;  // 16-byte vectors per row
-    uint4 xr[M][VPT];
-    float mx[M];
-#pragma unroll
-    for (int m = 0; m < M; ++m)
-#pragma unroll
-        for (int t = 0; t < VPT; ++t) {
-            const int v = threadIdx.x + t * T;
-            xr[m][t] = v < vpr ? xh4[m * vpr + v] : make_uint4(0, 0, 0, 0);
-        }
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-        mx[m] = 0.0f;
-#pragma unroll
-        for (int t = 0; t < VPT; ++t) {
-            const uint32_t wd[4] = {xr[m][t].x, xr[m][t].y, xr[m][t].z, xr[m][t].w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 f = __half22float2(u32_as_h2(wd[e]));
-                mx[m] = fmaxf(mx[m], fmaxf(fabsf(f.x), fabsf(f.y)));
-            }
-        }
-    }
-#pragma unroll
-    for (int m = 0; m < M; ++m)
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], o));
-    __shared__ float red_m[kW8Warps][M];
-    __shared__ float inv_s[M];
-    if (lane == 0) {
-#pragma unroll
-        for (int m = 0; m < M; ++m) red_m[warp][m] = mx[m];
-    }
-    __syncthreads();
-    if (threadIdx.x < M) {
-        const int m = threadIdx.x;
-        float r = 0.0f;
-        for (int i = 0; i < kW8Warps; ++i) r = fmaxf(r, red_m[i][m]);
-        const float scale = scale_from_absmax(r);
-        inv_s[m] = __fdiv_rn(1.0f, scale);
-        const __half sh = __float2half_rn(scale);
-        xscale_s[m] = __half2float(sh);
-        if (blockIdx.x == 0 && a.xs_out) a.xs_out[m] = sh;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-        const float inv = inv_s[m];
-#pragma unroll
-        for (int t = 0; t < VPT; ++t) {
-            const int v = threadIdx.x + t * T;
-            if (v >= vpr) continue;
-            const uint32_t wd[4] = {xr[m][t].x, xr[m][t].y, xr[m][t].z, xr[m][t].w};
-            uint32_t packed[2] = {0u, 0u};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 f = __half22float2(u32_as_h2(wd[e]));
-                const uint32_t q0 = static_cast<uint8_t>(quant_act(f.x, inv));
-                const uint32_t q1 = static_cast<uint8_t>(quant_act(f.y, inv));
-                packed[e >> 1] |= (q0 | (q1 << 8)) << (16 * (e & 1));
-            }
-            *reinterpret_cast<uint2*>(xq8 + m * stride + v * 8) = make_uint2(packed[0], packed[1]);
-            if (blockIdx.x == 0 && a.xq_out)
-                *reinterpret_cast<uint2*>(a.xq_out + static_cast<int64_t>(m) * a.K + v * 8) =
-                    make_uint2(packed[0], packed[1]);
-        }
-    }
+    quantize_rows_to_smem<M, VPT, kW8Warps * 32>(static_cast<const __half*>(a.x), a.K, xq8, stride, xscale_s,
+                                                 a.xq_out, a.xs_out);
 }
 
 template <int M, int KCH, bool FUSED>
@@ -470,18 +386,20 @@ __global__ void quantize_weight_kernel(const __half* __restrict__ w, int8_t* __r
     pdl_wait();
     const int n = blockIdx.x * blockDim.x + threadIdx.x;
     if (n >= N) return;
+    // layout 2 reads row n of an [N][K] weight; 0 and 1 read column n of [K][N]
+    auto in = [&](int k) { return layout == 2 ? w[static_cast<int64_t>(n) * K + k] : w[static_cast<int64_t>(k) * N + n]; };
     float mx = 0.0f;
-    for (int k = 0; k < K; ++k) mx = fmaxf(mx, fabsf(__half2float(w[static_cast<int64_t>(k) * N + n])));
+    for (int k = 0; k < K; ++k) mx = fmaxf(mx, fabsf(__half2float(in(k))));
     const float scale = scale_from_absmax(mx);
     const float inv = __fdiv_rn(1.0f, scale);
     w_scale[n] = __ushort_as_half(f32_to_f16_trunc(scale));
     for (int k = 0; k < K; ++k) {
-        float q = __fmul_rn(__half2float(w[static_cast<int64_t>(k) * N + n]), inv);
+        float q = __fmul_rn(__half2float(in(k)), inv);
         q = q > 127.0f ? 127.0f : q;
         q = q < -128.0f ? -128.0f : q;
         q = q >= 0.0f ? __fadd_rn(q, 0.5f) : __fsub_rn(q, 0.5f);
         const int8_t v = static_cast<int8_t>(__float2int_rz(q));
-        if (layout == 0) wq[static_cast<int64_t>(n) * K + k] = v;
+        if (layout != 1) wq[static_cast<int64_t>(n) * K + k] = v;
         else wq[static_cast<int64_t>(k) * N + n] = v;
     }
 }
@@ -666,7 +584,7 @@ int mcv_w8a8_quantize_weight(const void* w_kn, void* wq, void* w_scale, int64_t 
                              mcv_stream_t stream) {
     if (!w_kn || !wq || !w_scale) return fail(MCV_ERR_NULL, "w8a8_quantize_weight: null pointer");
     if (K < 1 || N < 1 || K > (1 << 30) || N > (1 << 30)) return fail(MCV_ERR_SHAPE, "w8a8_quantize_weight: bad shape");
-    if (w_layout != 0 && w_layout != 1) return fail(MCV_ERR_VALUE, "w8a8_quantize_weight: w_layout must be 0 or 1");
+    if (w_layout < 0 || w_layout > 2) return fail(MCV_ERR_VALUE, "w8a8_quantize_weight: w_layout must be 0, 1 or 2");
     return launch(quantize_weight_kernel, dim3(static_cast<unsigned>((N + 127) / 128)), dim3(128), 0,
                   static_cast<cudaStream_t>(stream), static_cast<const __half*>(w_kn), static_cast<int8_t*>(wq),
                   static_cast<__half*>(w_scale), static_cast<int>(K), static_cast<int>(N), w_layout);

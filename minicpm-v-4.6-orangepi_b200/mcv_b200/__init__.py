@@ -71,6 +71,7 @@ _SIGS = {
     "mcv_w8a8_dequant": [_vp, _vp, _vp, _vp, _i64, _i64, _vp],
     "mcv_w8a8_fused": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
     "mcv_w8a8_quantize_weight": [_vp, _vp, _vp, _i64, _i64, _int, _vp],
+    "mcv_lm_head_argmax_w8a8": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _sz, _vp],
     "mcv_set_w8a8_decode_mode": [ctypes.c_char_p],
     "mcv_w8a8_decode_enabled": [],
     "mcv_w8a8_policy_allows": [ctypes.c_char_p],
@@ -462,8 +463,21 @@ def w8a8_fused(x, w_int8, w_scale, out, acc=None, x_int8=None, x_scale=None, w_l
                                 _ptr(x_scale), M, K, N, w_layout, _stream(stream)), "w8a8_fused")
 
 
+def lm_head_argmax_w8a8(x, w_int8, w_scale, workspace, out_index=None, out_key=None, n_offset: int = 0,
+                        stream=None) -> None:
+    """W8A8 lm_head + greedy argmax over int8 rows w_int8 [N_shard, K] with
+    fp16 per-row scales (mcv_lm_head_argmax_w8a8)."""
+    M, K = x.shape
+    N = w_int8.shape[0]
+    _check(lib().mcv_lm_head_argmax_w8a8(_ptr(x), _ptr(w_int8), _ptr(w_scale), _ptr(out_key), _ptr(out_index), M, K,
+                                         N, n_offset, _ptr(workspace), workspace.numel(), _stream(stream)),
+           "lm_head_argmax_w8a8")
+
+
 def quantize_dense_weight_w8a8(w_kn, wq, w_scale, w_layout: int = 0, stream=None) -> None:
-    K, N = w_kn.shape
+    """Per-channel int8 quantization (mcv_w8a8_quantize_weight); w_layout 2
+    takes the weight as [N, K] (e.g. the embedding), 0 and 1 as [K, N]."""
+    K, N = w_kn.shape if w_layout != 2 else w_kn.shape[::-1]
     _check(lib().mcv_w8a8_quantize_weight(_ptr(w_kn), _ptr(wq), _ptr(w_scale), K, N, w_layout, _stream(stream)),
            "quantize_dense_weight_w8a8")
 

@@ -225,3 +225,40 @@ def test_lm_head_greedy_host_refuses_device_x(cuda):
                                    ctypes.c_void_p(host_idx.data_ptr()), 1, 1024, 64, 0, 0,
                                    ctypes.c_void_p(ws.data_ptr()), ws.numel(), None)
     assert st == 7 and b"host memory" in L.mcv_last_error()
+
+
+@pytest.mark.parametrize("M", [1, 3])
+def test_lm_head_w8a8_matches_reference_scan(cuda, M):
+    """W8A8 lm_head: the embedding quantized per row on the GPU (layout 2 =
+    the oracle's per-channel quantization of its transpose, bit for bit),
+    then the fused kernel's index equals the reference's scan - fp16 logits
+    RN((acc*ws)*xs), subnormals read as zero, strict '>' first max."""
+    import mcv_b200 as mcv
+    torch = cuda
+    K, V = 1024, 24000
+    r = np.random.default_rng(30 + M)
+    emb = (r.standard_normal((V, K)) * 0.02).astype(np.float16)
+    x = r.standard_normal((M, K)).astype(np.float16)
+    ed = torch.from_numpy(emb).cuda()
+    wq = torch.empty((V, K), dtype=torch.int8, device="cuda")
+    ws = torch.empty(V, dtype=torch.float16, device="cuda")
+    mcv.quantize_dense_weight_w8a8(ed, wq, ws, w_layout=2)
+    torch.cuda.synchronize()
+    wq_ref, ws_ref = oracle.quantize_dense_weight_w8a8(emb.T.copy())
+    assert np.array_equal(wq.cpu().numpy(), np.ascontiguousarray(wq_ref.T))
+    assert np.array_equal(ws.cpu().numpy().view(np.uint16), np.asarray(ws_ref).view(np.uint16).reshape(-1))
+
+    work = mcv.lm_head_workspace(M)
+    idx = torch.empty(M, dtype=torch.int64, device="cuda")
+    key = torch.empty(M, dtype=torch.int64, device="cuda")
+    for _ in range(2):  # the workspace is left ready for the next call
+        mcv.lm_head_argmax_w8a8(torch.from_numpy(x).cuda(), wq, ws, work, out_index=idx, out_key=key)
+        torch.cuda.synchronize()
+        _, bits = oracle.w8a8_fused(x, wq_ref, ws_ref, nthreads=8)
+        bits = np.asarray(bits).reshape(M, V)
+        for m in range(M):
+            b = bits[m]
+            vals = oracle.f16_to_f32(b)
+            vals = np.where(((b >> 10) & 0x1F) == 0, np.float32(0.0), vals)  # host h2f: subnormals -> 0
+            want = int(np.argmax(vals))  # first maximum = the strict '>' scan (no NaN from int8 dots)
+            assert int(idx[m].item()) == want, (m, int(idx[m].item()), want)

@@ -78,7 +78,7 @@ def test_w8a8_arguments(L):
     assert L.mcv_w8a8_fused(F2, F, F, F, None, None, None, 1, 1024, 3584, 0, None) == ALIGN
     assert L.mcv_w8a8_fused(None, F, F, F, None, None, None, 1, 1024, 3584, 0, None) == NULL
     assert L.mcv_w8a8_quantize(F, F, F, 0, 1024, None) == SHAPE
-    assert L.mcv_w8a8_quantize_weight(F, F, F, 1024, 3584, 2, None) == VALUE
+    assert L.mcv_w8a8_quantize_weight(F, F, F, 1024, 3584, 3, None) == VALUE
 
 
 def test_decode_dispatch_arguments(L):
