@@ -101,3 +101,15 @@ def test_context_set_up_arguments(L):
     comm = ctypes.c_void_p()
     uid = ctypes.create_string_buffer(int(L.mcv_nccl_unique_id_bytes()))
     assert L.mcv_nccl_comm_init(ctypes.byref(comm), 2, uid, 5) == VALUE
+
+
+def test_lm_head_w8a8_arguments(L):
+    h = L.mcv_lm_head_argmax_w8a8
+    ws_bytes = L.mcv_lm_head_workspace_size(1)
+    assert h(F, F, None, None, F, 1, 1024, 1000, 0, F, ws_bytes, None) == NULL       # scales
+    assert h(F, F, F, None, None, 1, 1024, 1000, 0, F, ws_bytes, None) == NULL       # no output
+    assert h(F, F, F, None, F, 1, 1032, 1000, 0, F, ws_bytes, None) == SHAPE         # K % 16
+    assert h(F, F, F, None, F, 1, 8192, 1000, 0, F, ws_bytes, None) == SHAPE         # K <= 4096
+    assert h(F, F, F, None, F, 9, 1024, 1000, 0, F, ws_bytes, None) == SHAPE         # M
+    assert h(F, F, F, None, F, 1, 1024, 1000, 0, F, ws_bytes - 1, None) == WORKSPACE
+    assert h(F2, F, F, None, F, 1, 1024, 1000, 0, F, ws_bytes, None) == ALIGN
