@@ -190,6 +190,25 @@ int64_t lm_head_greedy_index(const T& x, const T& embed, void* workspace, size_t
     return idx;
 }
 
+/* The W8A8 branch of lm_head_greedy (language_model.cpp:430-479): int8
+ * embedding rows `embed_int8` [V,K] with fp16 per-row scales `embed_scale`
+ * (mcv_w8a8_quantize_weight, w_layout 2), x quantized in the kernel; index
+ * read back as above. */
+template <class T>
+int64_t lm_head_greedy_index_w8a8(const T& x, const T& embed_int8, const T& embed_scale, void* workspace,
+                                  size_t workspace_bytes, void* index_dev, cudaStream_t stream) {
+    detail::need_rank2(x, "lm_head_greedy_index_w8a8");
+    detail::need_rank2(embed_int8, "lm_head_greedy_index_w8a8");
+    check(mcv_lm_head_argmax_w8a8(x.data(), embed_int8.data(), embed_scale.data(), nullptr, index_dev, 1,
+                                  x.shape()[1], embed_int8.shape()[0], 0, workspace, workspace_bytes, stream),
+          "lm_head_greedy_index_w8a8");
+    int64_t idx = -1;
+    cudaError_t e = cudaMemcpyAsync(&idx, index_dev, sizeof(idx), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("lm_head_greedy_index_w8a8: ") + cudaGetErrorString(e));
+    return idx;
+}
+
 }  // namespace mcv_ops
 
 #endif

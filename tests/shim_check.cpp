@@ -44,6 +44,9 @@ int main() {
     bad += expect_status([&] { mcv_ops::w8a8_quantize(flat, out, out, s); }, MCV_ERR_SHAPE, "1-D input");
     bad += expect_status([&] { mcv_ops::matmul_decode_dispatch<FakeTensor>(x, nullptr, nullptr, nullptr, out, s); },
                          MCV_ERR_NULL, "no formats");
+    FakeTensor emb8{nullptr, {1000, 1024}}, emb_scale{nullptr, {1000}};
+    bad += expect_status([&] { mcv_ops::lm_head_greedy_index_w8a8(x, emb8, emb_scale, nullptr, 0, nullptr, s); },
+                         MCV_ERR_NULL, "w8a8 lm_head, null scales");
     if (bad == 0) std::printf("shim ok\n");
     return bad;
 }
