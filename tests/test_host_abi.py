@@ -193,3 +193,36 @@ def test_tuning_keys_round_trip_and_reject_unknown():
         assert lib.mcv_get_tuning(key) == 0
     assert lib.mcv_set_tuning(count, 1) != 0
     assert lib.mcv_set_tuning(0, 1) != 0
+
+
+try:
+    from hypothesis import HealthCheck, given, settings
+    from hypothesis import strategies as st
+except ImportError:  # pragma: no cover
+    given = None
+
+
+if given is not None:
+    @settings(max_examples=25, deadline=None, suppress_health_check=[HealthCheck.function_scoped_fixture])
+    @given(kg=st.integers(1, 8), n8=st.integers(1, 40), seed=st.integers(0, 2**31 - 1))
+    def test_packers_round_trip_any_shape(host_pack, kg, n8, seed):
+        """Random shapes (K = 128 kg, N = 8 n8: ragged strips included): the
+        logical, GPTQ and AWQ packers all decode to the oracle's (q - zero)
+        and keep the scales exactly."""
+        K, N = 128 * kg, 8 * n8
+        r = np.random.default_rng(seed)
+        q = r.integers(0, 16, (K, N), dtype=np.uint8)
+        z = r.integers(0, 16, (kg, N), dtype=np.uint8)
+        s = r.uniform(0.002, 0.02, (kg, N)).astype(np.float16)
+        w = mcv_b200.pack_w4a16(q, z, s)
+        got, sc = decode_layout(w)
+        assert np.array_equal(got, oracle.w4a16_fold_zeros(q, z).astype(np.int16))
+        assert np.array_equal(sc, s.view(np.uint16))
+        qa, za = synth.awq_pack(q, z)
+        got_a, _ = decode_layout(mcv_b200.pack_w4a16_awq(qa, za, s))
+        assert np.array_equal(got_a, oracle.unpack_awq(qa, za).astype(np.int16))
+        zg = (z + 1).astype(np.uint8)  # GPTQ stores zero - 1
+        qg, zgp = synth.gptq_pack(q, np.minimum(zg, 16))
+        gidx = (np.arange(K) // 128).astype(np.int32)
+        got_g, _ = decode_layout(mcv_b200.pack_w4a16_gptq(qg, zgp, gidx, s))
+        assert np.array_equal(got_g, oracle.unpack_gptq(qg, zgp, gidx, kg).astype(np.int16))
