@@ -405,6 +405,16 @@ def run_profile(args):
         out = torch.empty((args.gemm_m, 4096), dtype=torch.float16, device="cuda")
         for _ in range(5):
             mcv.matmul_w4a16_gemm(x, w, out)
+    elif args.profile == "lm_head_w8a8":
+        w = rand_f16(torch, (args.rows, K_HIDDEN), 0.02, gen)
+        wq = torch.empty((args.rows, K_HIDDEN), dtype=torch.int8, device="cuda")
+        wsc = torch.empty(args.rows, dtype=torch.float16, device="cuda")
+        mcv.quantize_dense_weight_w8a8(w, wq, wsc, w_layout=2)
+        x = rand_f16(torch, (1, K_HIDDEN), 1.0, gen)
+        ws = mcv.lm_head_workspace(1)
+        idx = torch.empty(1, dtype=torch.int64, device="cuda")
+        for _ in range(5):
+            mcv.lm_head_argmax_w8a8(x, wq, wsc, ws, out_index=idx)
     elif args.profile == "w8a8":
         for M in (1, 8):
             x, w8, ws8 = synth.w8a8_inputs(M, 1024, 3584, seed=2)
@@ -426,10 +436,10 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the config 0/2/3 sub-benchmarks")
     ap.add_argument("--collective", default="p2p", choices=["p2p", "nccl"],
                     help="N>1: fused peer-mailbox exchange inside the kernel, or a separate NCCL all-reduce")
-    ap.add_argument("--profile", choices=["lm_head", "w4a16", "w4a16_grouped", "w8a8", "gemm"],
+    ap.add_argument("--profile", choices=["lm_head", "lm_head_w8a8", "w4a16", "w4a16_grouped", "w8a8", "gemm"],
                     help="run a few untimed launches of one kernel family (a small case for ncu)")
     ap.add_argument("--gemm-m", type=int, default=1024, help="--profile gemm: activation rows M")
-    ap.add_argument("--rows", type=int, default=65536, help="--profile lm_head: vocab rows (65536 = 128 MB)")
+    ap.add_argument("--rows", type=int, default=65536, help="--profile lm_head / lm_head_w8a8: vocab rows (65536 = 128 MB fp16)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
