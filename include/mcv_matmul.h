@@ -220,7 +220,10 @@ size_t mcv_lm_head_workspace_size(int64_t M);
  * Logits are fp32 dots; ties go to the smallest index (the first maximum,
  * language_model.cpp:475 and tests/test_lm_head_pipeline.cpp:104).
  * fp16_logits = 1 compares logits rounded to fp16, as the production
- * lm_head_greedy does on its D2H-copied fp16 chunk (language_model.cpp:471-479).
+ * lm_head_greedy does on its D2H-copied fp16 chunk (language_model.cpp:471-479);
+ * unlike that host scan it keeps fp16 subnormals instead of reading them as
+ * zero, which can only matter when the largest logit is below 6.1e-5 in
+ * magnitude.  (mcv_lm_head_argmax_w8a8 reads them as zero, as the scan does.)
  * Replaces the per-chunk matmul + D2H + host argmax loop of lm_head_greedy,
  * src/csrc/lib/language_model.cpp:464-480. */
 int mcv_lm_head_argmax(const void* x, const void* w, void* out_key, void* out_index, int64_t M,
