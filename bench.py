@@ -129,6 +129,10 @@ def run_reference(args):
         oracle.lm_head_argmax(x, w, nthreads=nthreads)
     dt = (time.perf_counter() - t0) / args.steps
     us = dt * 1e6
+    # the single-thread variant: one full scan, exactly the reference loop order
+    t0 = time.perf_counter()
+    oracle.lm_head_argmax(x, w, nthreads=1)
+    us1 = (time.perf_counter() - t0) * 1e6
     line = {
         "impl": "reference", "metric": METRIC, "value": round(us, 2), "unit": "us", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4),
@@ -137,7 +141,9 @@ def run_reference(args):
         "cpu_baseline": {"value": round(us, 2), "unit": "us", "cores": nthreads, "kind": "port",
                          "sample": "full 248094-row vocab per step: fp32 dot over ascending k and strict '>' "
                                    "first-max argmax (tests/test_lm_head_pipeline.cpp:95-107), "
-                                   f"rows split over {nthreads} threads"},
+                                   f"rows split over {nthreads} threads",
+                         "single_thread": {"value": round(us1, 1), "unit": "us", "cores": 1,
+                                           "sample": "one full-vocabulary scan on one thread"}},
         "e2e": {"value": round(us, 2), "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -465,18 +471,22 @@ def main():
     l2 = int(getattr(props, "L2_cache_size", 126 * 1024 * 1024))
 
     # ---- shard of the vocabulary ----
+    # Every rank draws the same seeded full-vocabulary weight and keeps its
+    # contiguous row range, so the sharded answer can be checked against the
+    # CPU oracle over the whole vocabulary on rank 0.
     per = (VOCAB + world - 1) // world
     a, b = rank * per, min(VOCAB, (rank + 1) * per)
     rows = b - a
     gen = torch.Generator(device="cuda")
-    gen.manual_seed(1234 + rank)
+    gen.manual_seed(1234)
     shard_bytes = rows * K_HIDDEN * 2
     copies = max(1, int(np.ceil(2 * l2 / shard_bytes)))
-    w_copies = [rand_f16(torch, (rows, K_HIDDEN), 0.02, gen)]
-    w_copies += [w_copies[0].clone() for _ in range(copies - 1)]
+    w_full = rand_f16(torch, (VOCAB, K_HIDDEN), 0.02, gen)
     x = rand_f16(torch, (1, K_HIDDEN), 1.0, gen)
-    if world > 1:
-        dist.broadcast(x, 0)
+    w_copies = [w_full[a:b].clone()]
+    w_copies += [w_copies[0].clone() for _ in range(copies - 1)]
+    w_full_host = w_full.cpu().numpy() if rank == 0 else None
+    del w_full
     ws = mcv.lm_head_workspace(1)
     key = torch.empty(1, dtype=torch.int64, device="cuda")
     idx = torch.empty(1, dtype=torch.int64, device="cuda")
@@ -581,30 +591,50 @@ def main():
     us_step = ms_main / args.steps * 1e3
     us_kern = ms_kern / args.steps * 1e3
 
+    # ---- parity of the (sharded) answer: one more step through the same
+    # path, every rank's index gathered on rank 0 and compared with the CPU
+    # oracle over the full vocabulary ----
+    idx.fill_(-2)
+    one_step(0)
+    torch.cuda.synchronize()
+    if comm is None and p2p is None:
+        gpu_idx = [int(idx.item())]
+    else:
+        all_idx = [torch.empty_like(idx) for _ in range(world)]
+        dist.all_gather(all_idx, idx)
+        gpu_idx = [int(t.item()) for t in all_idx]
+
     extras = {}
     cpu_baseline = None
-    if rank == 0 and world == 1:
+    if rank == 0:
         # CPU baseline: the oracle (a C port of the reference's CPU checker) on this host's cores
         import oracle
         nthreads = os.cpu_count() or 1
         xh = x.cpu().numpy()
-        wh = w_copies[0].cpu().numpy()
-        oracle.lm_head_argmax(xh, wh, nthreads=nthreads)
+        oracle.lm_head_argmax(xh, w_full_host, nthreads=nthreads)
         reps = []
         for _ in range(3):
             t0 = time.perf_counter()
-            ci, _, _ = oracle.lm_head_argmax(xh, wh, nthreads=nthreads)
+            ci, cbest, cgap = oracle.lm_head_argmax(xh, w_full_host, nthreads=nthreads)
             reps.append(time.perf_counter() - t0)
         cpu_us = statistics.median(reps) * 1e6
+        t0 = time.perf_counter()
+        ci1, _, _ = oracle.lm_head_argmax(xh, w_full_host, nthreads=1)
+        cpu1_us = (time.perf_counter() - t0) * 1e6
         cpu_baseline = {"value": round(cpu_us, 1), "unit": "us", "cores": nthreads, "kind": "port",
                         "sample": "the full 248094-row lm_head + argmax of this run's weights, median of 3, "
                                   "fp32 ascending-k dots (tests/test_lm_head_pipeline.cpp:95-107) "
-                                  f"split over {nthreads} threads"}
-        mcv.lm_head_argmax(x, w_copies[0], ws, out_index=idx)
-        extras["parity_check"] = {"gpu_index": int(idx.item()), "cpu_index": int(ci[0]),
-                                  "match": int(idx.item()) == int(ci[0])}
-        del wh
-        if not args.no_extras:
+                                  f"split over {nthreads} threads",
+                        "single_thread": {"value": round(cpu1_us, 1), "unit": "us", "cores": 1,
+                                          "sample": "the same full-vocabulary scan once on one thread, "
+                                                    "exactly the reference loop order"}}
+        extras["parity_check"] = {"gpu_index": gpu_idx[0], "gpu_index_per_rank": gpu_idx,
+                                  "cpu_index": int(ci[0]), "cpu_index_single_thread": int(ci1[0]),
+                                  "top2_gap": float(cgap[0]), "best_logit": float(cbest[0]),
+                                  "match": all(g == int(ci[0]) for g in gpu_idx) and int(ci1[0]) == int(ci[0]),
+                                  "oracle": "full-vocabulary fp32 scan of the same seeded weight, strict '>'"}
+        del w_full_host
+        if world == 1 and not args.no_extras:
             extras["w4a16_gemv"] = bench_w4a16_gemv(torch, mcv, synth, l2, hbm)
             extras["w8a8"] = bench_w8a8(torch, mcv, synth, l2, hbm)
             extras["decode_step"] = bench_decode_step(torch, mcv, synth, hbm, w_copies[0], ws)

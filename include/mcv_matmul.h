@@ -247,13 +247,16 @@ int mcv_argmax_last_dim_f16(const void* logits, void* out_index, int64_t M, int6
  * stream capture.  Each call clears the array with cudaMemsetAsync on `stream` and
  * allocates nothing.  All calls share the one array: calls that
  * may overlap on the GPU (other streams, other threads) race and must be
- * serialised by the caller. */
+ * serialised by the caller.  The looked-up address is kept for the life of the
+ * process: a cudaDeviceReset of a device this entry point has run on is not
+ * supported (the next call would use the old address). */
 size_t mcv_lm_head_noalloc_max_bytes(void);
 int mcv_lm_head_argmax_noalloc(const void* x, const void* w, void* out_key, void* out_index,
                                int64_t M, int64_t K, int64_t N_shard, int64_t n_offset,
                                int fp16_logits, mcv_stream_t stream);
 
-/* int64 index[m] = 0xFFFFFFFF - (uint32)key[m]: decode argmax keys on the device. */
+/* int64 index[m] = 0xFFFFFFFF - (uint32)key[m]: decode argmax keys on the device
+ * (key 0, "no row", decodes to -1). */
 int mcv_argmax_key_to_index(const void* key, void* out_index, int64_t M, mcv_stream_t stream);
 
 /* ---- sharded lm_head across GPUs (one process per GPU, NCCL over NVLink) -- */
@@ -384,6 +387,11 @@ int mcv_w8a8_quantize_weight(const void* w_kn, void* wq, void* w_scale, int64_t 
  *   lm_head). */
 int mcv_set_w8a8_decode_mode(const char* mode);
 int mcv_w8a8_decode_enabled(void);
+/* The per-layer decode gate that mcv_matmul_decode_dispatch applies
+ * (decoder_layer.cpp:19-25): the variable is set (an empty value counts)
+ * and is neither "0" nor "false".  It differs from mcv_w8a8_decode_enabled
+ * only for a set-but-empty variable, exactly as the reference's two rules do. */
+int mcv_w8a8_decode_gate_enabled(void);
 int mcv_w8a8_policy_allows(const char* token);
 /* The same rule for an explicit mode string (no process state). */
 int mcv_w8a8_policy_allows_mode(const char* mode, const char* token);

@@ -151,10 +151,13 @@ __device__ __forceinline__ uint64_t warp_max_u64(uint64_t v) {
 
 // Order-preserving argmax key: larger logit -> larger key; equal logits ->
 // smaller index wins.  -0 is folded into +0 so it ties with +0 like a float
-// comparison does.
+// comparison does.  A NaN logit gets the lowest ordered value (below -inf),
+// so it never beats a number: the reference's scan `v > best` is false for
+// every NaN (src/csrc/lib/language_model.cpp:474-477).
 __device__ __forceinline__ uint64_t argmax_key(float logit, uint32_t index) {
     uint32_t u = __float_as_uint(logit + 0.0f);
     u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    if (logit != logit) u = 0u;
     return (static_cast<uint64_t>(u) << 32) | static_cast<uint64_t>(0xffffffffu - index);
 }
 

@@ -383,7 +383,8 @@ __global__ void key_to_index_kernel(const uint64_t* __restrict__ key, int64_t* _
     pdl_trigger();
     pdl_wait();
     const int m = threadIdx.x;
-    if (m < M) out[m] = static_cast<int64_t>(0xffffffffu - static_cast<uint32_t>(key[m] & 0xffffffffu));
+    // key 0 means "no row" (every shard empty): -1, as finish_argmax reports it
+    if (m < M) out[m] = key[m] == 0 ? -1 : static_cast<int64_t>(0xffffffffu - static_cast<uint32_t>(key[m] & 0xffffffffu));
 }
 
 int row_grid(int64_t N) {

@@ -19,16 +19,31 @@ namespace {
 
 std::mutex g_policy_mu;
 bool g_policy_loaded = false;
+bool g_policy_set = false;  // the variable exists (possibly empty)
 std::string g_policy_mode;
 
-std::string policy_mode() {
-    std::lock_guard<std::mutex> lock(g_policy_mu);
+void load_policy_locked() {
     if (!g_policy_loaded) {
         const char* v = std::getenv("MINICPM_W8A8_DECODE");
         g_policy_mode = v ? v : "";
+        g_policy_set = v != nullptr;
         g_policy_loaded = true;
     }
+}
+
+std::string policy_mode() {
+    std::lock_guard<std::mutex> lock(g_policy_mu);
+    load_policy_locked();
     return g_policy_mode;
+}
+
+// decoder_layer.cpp:19-25: the per-layer decode gate is "set, and neither
+// "0" nor "false"", so a set-but-empty variable turns W8A8 decode on there,
+// while language_model.cpp:27-30 (the lm_head policy) treats it as off.
+bool decode_gate_enabled() {
+    std::lock_guard<std::mutex> lock(g_policy_mu);
+    load_policy_locked();
+    return g_policy_set && g_policy_mode != "0" && g_policy_mode != "false";
 }
 
 // language_model.cpp:27-30
@@ -54,6 +69,7 @@ int mcv_set_w8a8_decode_mode(const char* mode) {
     std::lock_guard<std::mutex> lock(g_policy_mu);
     if (mode) {
         g_policy_mode = mode;
+        g_policy_set = true;
         g_policy_loaded = true;
     } else {
         g_policy_loaded = false;  // back to the environment on the next query
@@ -62,6 +78,8 @@ int mcv_set_w8a8_decode_mode(const char* mode) {
 }
 
 int mcv_w8a8_decode_enabled(void) { return mode_enabled(policy_mode()) ? 1 : 0; }
+
+int mcv_w8a8_decode_gate_enabled(void) { return decode_gate_enabled() ? 1 : 0; }
 
 int mcv_w8a8_policy_allows(const char* token) {
     if (!token) return 0;
@@ -77,9 +95,9 @@ int mcv_matmul_decode_dispatch(const void* x, const mcv_decode_weights* w, void*
                                int64_t N, mcv_stream_t stream) {
     if (!x || !w || !out) return fail(MCV_ERR_NULL, "matmul_decode_dispatch: null pointer");
     if (M < 1) return fail(MCV_ERR_SHAPE, "matmul_decode_dispatch: M must be >= 1");
-    // decoder_layer.cpp:212-214, 232: W8A8 when the policy is on, the weight
-    // exists and the input is one row
-    const bool w8_ready = mode_enabled(policy_mode()) && w->w8_weight != nullptr && w->w8_scale != nullptr;
+    // decoder_layer.cpp:212-214, 232: W8A8 when the decode gate is on, the
+    // weight exists and the input is one row
+    const bool w8_ready = decode_gate_enabled() && w->w8_weight != nullptr && w->w8_scale != nullptr;
     if (w8_ready && M == 1)
         return mcv_w8a8_fused(x, w->w8_weight, w->w8_scale, out, nullptr, nullptr, nullptr, M, K, N, 0, stream);
     // decoder_layer.cpp:239-242: W4A16 for one row; more rows go to the

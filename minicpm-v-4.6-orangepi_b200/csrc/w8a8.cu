@@ -380,9 +380,12 @@ __device__ __forceinline__ uint16_t f32_to_f16_trunc(float f) {
 }
 
 // One thread per output column n; reads the [K][N] fp16 source coalesced.
+// No early PDL trigger here: this kernel writes weights, and the GEMV kernels
+// read their weights before griddepcontrol.wait, so a dependent launch may only
+// start once every block of this one has finished its stores (the implicit
+// trigger at exit).
 __global__ void quantize_weight_kernel(const __half* __restrict__ w, int8_t* __restrict__ wq,
                                        __half* __restrict__ w_scale, int K, int N, int layout) {
-    pdl_trigger();
     pdl_wait();
     const int n = blockIdx.x * blockDim.x + threadIdx.x;
     if (n >= N) return;

@@ -74,6 +74,7 @@ _SIGS = {
     "mcv_lm_head_argmax_w8a8": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _sz, _vp],
     "mcv_set_w8a8_decode_mode": [ctypes.c_char_p],
     "mcv_w8a8_decode_enabled": [],
+    "mcv_w8a8_decode_gate_enabled": [],
     "mcv_w8a8_policy_allows": [ctypes.c_char_p],
     "mcv_w8a8_policy_allows_mode": [ctypes.c_char_p, ctypes.c_char_p],
     "mcv_matmul_decode_dispatch": [_vp, _vp, _vp, _i64, _i64, _i64, _vp],
@@ -511,6 +512,12 @@ def set_w8a8_decode_mode(mode) -> None:
 
 def w8a8_decode_enabled() -> bool:
     return bool(lib().mcv_w8a8_decode_enabled())
+
+
+def w8a8_decode_gate_enabled() -> bool:
+    """The gate matmul_decode_dispatch applies (decoder_layer.cpp:19-25):
+    a set-but-empty MINICPM_W8A8_DECODE counts as on."""
+    return bool(lib().mcv_w8a8_decode_gate_enabled())
 
 
 def w8a8_policy_allows(token: str, mode=None) -> bool:

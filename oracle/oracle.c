@@ -288,6 +288,7 @@ void orc_gemv_f16(const uint16_t* x, const uint16_t* w, int64_t M, int64_t K, in
 uint64_t orc_argmax_key(float logit, uint32_t index) {
     uint32_t u = f32_bits(logit + 0.0f);
     u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    if (logit != logit) u = 0u; /* NaN never wins a strict '>' scan */
     return ((uint64_t)u << 32) | (uint64_t)(0xffffffffu - index);
 }
 

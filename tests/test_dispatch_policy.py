@@ -44,12 +44,19 @@ def _in_fresh_process(env_mode, code):
     return out.stdout.strip()
 
 
-@pytest.mark.parametrize("env_mode", [None, "0", "false", "all", "selective", "mlp,full_q"])
+def expected_gate(env_mode):
+    """decoder_layer.cpp:19-25: set (even empty) and neither "0" nor "false"."""
+    return env_mode is not None and env_mode not in ("0", "false")
+
+
+@pytest.mark.parametrize("env_mode", [None, "", "0", "false", "all", "selective", "mlp,full_q"])
 def test_policy_from_environment(env_mode):
-    code = "print(int(m.w8a8_decode_enabled()), ''.join(str(int(m.w8a8_policy_allows(t))) for t in %r))" % TOKENS
+    code = ("print(int(m.w8a8_decode_enabled()), int(m.w8a8_decode_gate_enabled()), "
+            "''.join(str(int(m.w8a8_policy_allows(t))) for t in %r))" % TOKENS)
     got = _in_fresh_process(env_mode, code)
     mode = env_mode or ""
-    want = f"{int(mode not in ('', '0', 'false'))} " + "".join(str(int(expected(mode, t))) for t in TOKENS)
+    want = (f"{int(mode not in ('', '0', 'false'))} {int(expected_gate(env_mode))} "
+            + "".join(str(int(expected(mode, t))) for t in TOKENS))
     assert got == want
 
 

@@ -262,3 +262,54 @@ def test_lm_head_w8a8_matches_reference_scan(cuda, M):
             vals = np.where(((b >> 10) & 0x1F) == 0, np.float32(0.0), vals)  # host h2f: subnormals -> 0
             want = int(np.argmax(vals))  # first maximum = the strict '>' scan (no NaN from int8 dots)
             assert int(idx[m].item()) == want, (m, int(idx[m].item()), want)
+
+
+def test_lm_head_nan_row_never_wins(cuda):
+    """A row whose logit is NaN loses to every number, as in the reference's
+    strict '>' scan (language_model.cpp:474-477); the answer equals the
+    oracle's over the remaining rows."""
+    x, w = synth.lm_head_inputs(1024, 4096, seed=11)
+    ref_idx, _, _ = oracle.lm_head_argmax(x, w)
+    w = w.copy()
+    w[7, 3] = np.float16(np.nan)            # row 7's logit is NaN
+    w[int(ref_idx[0]) + 1, 0] = np.float16(np.nan)
+    ref2, _, _ = oracle.lm_head_argmax(x, w)
+    assert ref2[0] == ref_idx[0]
+    idx, _, _ = lm_head(cuda, x, w)
+    assert idx[0] == ref_idx[0]
+    # all-NaN but one finite row: the finite row wins
+    w3 = np.full((64, 1024), np.float16(np.nan), np.float16)
+    w3[40] = w[0]
+    ref3, _, _ = oracle.lm_head_argmax(x, w3)
+    idx3, _, _ = lm_head(cuda, x, w3)
+    assert ref3[0] == 40 and idx3[0] == 40
+
+
+def test_quantize_weight_then_lm_head_w8a8_same_stream(cuda):
+    """The weight quantizer followed directly by the W8A8 lm_head on one
+    stream, no synchronisation between: the lm_head reads its weights before
+    its dependency wait, so the quantizer must not release it early."""
+    import mcv_b200 as mcv
+    torch = cuda
+    K, V = 1024, 65536
+    r = np.random.default_rng(77)
+    x = r.standard_normal((1, K)).astype(np.float16)
+    xd = torch.from_numpy(x).cuda()
+    work = mcv.lm_head_workspace(1)
+    idx = torch.empty(1, dtype=torch.int64, device="cuda")
+    wq = torch.empty((V, K), dtype=torch.int8, device="cuda")
+    wsc = torch.empty(V, dtype=torch.float16, device="cuda")
+    for trial in range(3):
+        emb = (r.standard_normal((V, K)) * 0.02).astype(np.float16)
+        ed = torch.from_numpy(emb).cuda()
+        wq.fill_(0)
+        wsc.fill_(0)
+        torch.cuda.synchronize()
+        mcv.quantize_dense_weight_w8a8(ed, wq, wsc, w_layout=2)
+        mcv.lm_head_argmax_w8a8(xd, wq, wsc, work, out_index=idx)
+        torch.cuda.synchronize()
+        wq_ref, ws_ref = oracle.quantize_dense_weight_w8a8(emb.T.copy())
+        _, bits = oracle.w8a8_fused(x, wq_ref, ws_ref, nthreads=8)
+        b = np.asarray(bits).reshape(V)
+        vals = np.where(((b >> 10) & 0x1F) == 0, np.float32(0.0), oracle.f16_to_f32(b))
+        assert int(idx.item()) == int(np.argmax(vals)), trial
