@@ -194,6 +194,18 @@ typedef struct mcv_w4a16_problem {
 int mcv_w4a16_gemv_grouped(const mcv_w4a16_problem* problems, int count, int64_t M,
                            mcv_stream_t stream);
 
+/* The down projection with silu_mul fused into its activation load:
+ * out fp16 [M][N] = (silu(gate) * up) [M][K] . W over an mcv-int4 weight, with
+ * gate and up fp16 [M][K] (the gate/up projections' outputs).  The activation
+ * is formed per element as the silu_mul kernel does (fp32
+ * g / (1 + exp(-g)) * u, rounded to fp16; op_kernel/silu_mul_custom.cpp:63-72),
+ * so the result equals mcv_silu_mul followed by mcv_w4a16_gemv.  Replaces
+ * silu_mul + matmul_decode_dispatch(down) of decoder_layer.cpp:1203-1204.
+ * M = 1..8, K <= 8192 (multiple of 128), group 128. */
+int mcv_w4a16_gemv_silu_mul(const void* gate, const void* up, const void* qweight, const void* scales,
+                            const void* zeros, int zero_bias, void* out, int64_t M, int64_t K, int64_t N,
+                            int64_t group, mcv_stream_t stream);
+
 /* ======================================================================== */
 /* dense fp16 GEMV and the lm_head                                          */
 /* ======================================================================== */
@@ -229,6 +241,19 @@ size_t mcv_lm_head_workspace_size(int64_t M);
 int mcv_lm_head_argmax(const void* x, const void* w, void* out_key, void* out_index, int64_t M,
                        int64_t K, int64_t N_shard, int64_t n_offset, int fp16_logits,
                        void* workspace, size_t workspace_bytes, mcv_stream_t stream);
+
+/* lm_head_greedy's device half including its final rms_norm
+ * (src/csrc/lib/language_model.cpp:422-423): x is the raw last hidden state
+ * [M][K]; every block normalises it in its prologue (gamma fp16 [K],
+ * norm_variant 0 = the engine's rms_norm, ops.cpp:564-737: fp16 chain with
+ * (1 + gamma); 1 = the rms_norm1024 kernel's fp32 arithmetic with gamma), then
+ * the same GEMV + argmax as mcv_lm_head_argmax.  p2p_ctx NULL: this GPU's
+ * shard alone; else the peer exchange of mcv_lm_head_argmax_p2p.  Saves the
+ * separate normalisation launch and its 2 KB round trip per token. */
+int mcv_lm_head_argmax_rmsnorm(void* p2p_ctx, const void* x, const void* norm_gamma, float norm_eps,
+                               int norm_variant, const void* w, void* out_key, void* out_index, int64_t M,
+                               int64_t K, int64_t N_shard, int64_t n_offset, int fp16_logits, void* workspace,
+                               size_t workspace_bytes, mcv_stream_t stream);
 
 /* Greedy argmax of fp16 logits [M][V] -> int64 [M], first maximum wins.
  * Replaces argmax_last_dim (src/csrc/lib/ops.cpp:324-357, ops.h:21). */
@@ -301,8 +326,11 @@ int mcv_lm_head_argmax_p2p(void* ctx, const void* x, const void* w, void* out_ke
                            void* workspace, size_t workspace_bytes, mcv_stream_t stream);
 
 /* One greedy step from host memory to a host token id, as the reference's
- * lm_head_greedy hands the token back (src/csrc/lib/language_model.cpp:412-482;
- * its rms_norm stays with the caller): runs mcv_lm_head_argmax (p2p_ctx
+ * lm_head_greedy hands the token back (src/csrc/lib/language_model.cpp:412-482).
+ * norm_gamma (fp16 [K] on the device, may be NULL): the final rms_norm of
+ * language_model.cpp:423 (the engine's variant, eps norm_eps) runs in the
+ * kernel's prologue on the raw hidden state; NULL: x is already normalised.
+ * Runs mcv_lm_head_argmax (p2p_ctx
  * NULL) or mcv_lm_head_argmax_p2p (p2p_ctx from mcv_p2p_create/connect) on
  * this rank's rows for x (M rows, fp16, in host memory), hands the M int64
  * global indices to index_host and synchronises the stream.  x travels in
@@ -312,9 +340,10 @@ int mcv_lm_head_argmax_p2p(void* ctx, const void* x, const void* w, void* out_ke
  * directly; otherwise they go through index_dev (M int64 on the device) and a
  * copy.  x_dev and index_dev are required either way.  Synchronous; same
  * workspace rules as mcv_lm_head_argmax. */
-int mcv_lm_head_greedy_host(void* p2p_ctx, const void* x_host, void* x_dev, const void* w, void* index_dev,
-                            int64_t* index_host, int64_t M, int64_t K, int64_t N_shard, int64_t n_offset,
-                            int fp16_logits, void* workspace, size_t workspace_bytes, mcv_stream_t stream);
+int mcv_lm_head_greedy_host(void* p2p_ctx, const void* x_host, void* x_dev, const void* norm_gamma, float norm_eps,
+                            const void* w, void* index_dev, int64_t* index_host, int64_t M, int64_t K,
+                            int64_t N_shard, int64_t n_offset, int fp16_logits, void* workspace,
+                            size_t workspace_bytes, mcv_stream_t stream);
 
 /* ======================================================================== */
 /* W8A8: int8 activations (per-token absmax) x int8 weights (per channel)   */
@@ -371,6 +400,24 @@ int mcv_lm_head_argmax_w8a8(const void* x, const void* w_int8, const void* w_sca
  * Replaces quantize_dense_weight_w8a8 (src/csrc/lib/quantized_weight.cpp:231-268). */
 int mcv_w8a8_quantize_weight(const void* w_kn, void* wq, void* w_scale, int64_t K, int64_t N,
                              int w_layout, mcv_stream_t stream);
+
+/* ======================================================================== */
+/* The GEMVs' element-wise neighbours                                        */
+/* ======================================================================== */
+
+/* out fp16 [rows][H] = rms_norm(x fp16 [rows][H]) with gamma fp16 [H].
+ * variant 0: the engine's rms_norm (src/csrc/lib/ops.cpp:564-737): a chain
+ * of fp16 ops - x*x, mean, + eps, rsqrt, x * rstd, each rounded to fp16 -
+ * then times (1 + gamma); the mean's sum is exact.  variant 1: rms_norm1024
+ * (ops.cpp:536-562, op_kernel/rms_norm1024_custom.cpp:57-70): fp32
+ * x / sqrt(mean(x^2) + eps) * gamma, rounded once.  Any H (the custom
+ * kernel's fixed 1024 is not required). */
+int mcv_rms_norm(const void* x, const void* gamma, void* out, int64_t rows, int64_t H, float eps, int variant,
+                 mcv_stream_t stream);
+/* out = silu(gate) * up element-wise over n fp16 values (16-byte aligned):
+ * fp32 g / (1 + exp(-g)) * u rounded to fp16.  Replaces silu_mul
+ * (src/csrc/lib/ops.cpp:437-456, op_kernel/silu_mul_custom.cpp:63-72). */
+int mcv_silu_mul(const void* gate, const void* up, void* out, int64_t n, mcv_stream_t stream);
 
 /* ======================================================================== */
 /* Decode dispatch: which weight format a projection's matmul runs on        */

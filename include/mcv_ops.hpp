@@ -190,6 +190,49 @@ int64_t lm_head_greedy_index(const T& x, const T& embed, void* workspace, size_t
     return idx;
 }
 
+/* lm_head_greedy (language_model.cpp:412-482) as the engine calls it: the raw
+ * last hidden state [1,K], the final norm weight [K] (rms_norm of :423 fused
+ * into the kernel), the fp16 embedding rows [V,K]; returns the token id. */
+template <class T>
+int64_t lm_head_greedy(const T& last_hidden, const T& final_norm_w, const T& embed, double rms_epsilon,
+                       void* workspace, size_t workspace_bytes, void* index_dev, cudaStream_t stream) {
+    detail::need_rank2(last_hidden, "lm_head_greedy");
+    detail::need_rank2(embed, "lm_head_greedy");
+    if (final_norm_w.shape().size() != 1 || final_norm_w.shape()[0] != last_hidden.shape()[1])
+        throw Error(MCV_ERR_SHAPE, "lm_head_greedy: norm weight must be [hidden]");
+    check(mcv_lm_head_argmax_rmsnorm(nullptr, last_hidden.data(), final_norm_w.data(), static_cast<float>(rms_epsilon),
+                                     0, embed.data(), nullptr, index_dev, 1, last_hidden.shape()[1],
+                                     embed.shape()[0], 0, 0, workspace, workspace_bytes, stream),
+          "lm_head_greedy");
+    int64_t idx = -1;
+    cudaError_t e = cudaMemcpyAsync(&idx, index_dev, sizeof(idx), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("lm_head_greedy: ") + cudaGetErrorString(e));
+    return idx;
+}
+
+/* rms_norm (ops.h / ops.cpp:564-737): the engine's fp16 chain with (1 + gamma). */
+template <class T>
+void rms_norm(const T& x, const T& gamma, T& out, double epsilon, cudaStream_t stream, bool sync = false) {
+    if (x.shape().empty() || x.shape() != out.shape()) throw Error(MCV_ERR_SHAPE, "rms_norm: x/out shape mismatch");
+    const int64_t H = x.shape().back();
+    if (gamma.shape().size() != 1 || gamma.shape()[0] != H) throw Error(MCV_ERR_SHAPE, "rms_norm: gamma must be [H]");
+    int64_t rows = 1;
+    for (size_t i = 0; i + 1 < x.shape().size(); ++i) rows *= x.shape()[i];
+    check(mcv_rms_norm(x.data(), gamma.data(), out.data(), rows, H, static_cast<float>(epsilon), 0, stream), "rms_norm");
+    finish(stream, sync, "rms_norm");
+}
+
+/* silu_mul (ops.h:41, ops.cpp:437-456). */
+template <class T>
+void silu_mul(const T& gate, const T& up, T& out, cudaStream_t stream, bool sync = false) {
+    if (gate.shape() != up.shape() || gate.shape() != out.shape()) throw Error(MCV_ERR_SHAPE, "silu_mul shape mismatch");
+    int64_t n = 1;
+    for (int64_t d : gate.shape()) n *= d;
+    check(mcv_silu_mul(gate.data(), up.data(), out.data(), n, stream), "silu_mul");
+    finish(stream, sync, "silu_mul");
+}
+
 /* The W8A8 branch of lm_head_greedy (language_model.cpp:430-479): int8
  * embedding rows `embed_int8` [V,K] with fp16 per-row scales `embed_scale`
  * (mcv_w8a8_quantize_weight, w_layout 2), x quantized in the kernel; index

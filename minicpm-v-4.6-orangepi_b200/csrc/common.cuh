@@ -93,6 +93,26 @@ struct P2PArgs {
     int rank, nranks;
 };
 
+// rms_norm applied to the activation rows in a kernel's prologue (see
+// neighbours.cuh for the arithmetic).
+struct NormArgs {
+    const __half* gamma;  // null: no normalisation
+    float eps;
+    int variant;          // 0: the engine's fp16 chain with (1 + gamma); 1: the fp32 kernel with gamma
+};
+
+// The fused lm_head GEMV + argmax (dense.cu), shared by every lm_head entry
+// point.  p2p (may be null): cross-GPU exchange in the last block.  x_param
+// (host memory, may be null): when set and M * K <= 2048, x rides in the
+// launch parameters and `x` is not read.  norm (may be null): rms_norm of x
+// first.
+int lm_head_argmax_impl_p2p(const void* x, const void* w, void* out_key, void* out_index, int64_t M, int64_t K,
+                            int64_t N, int64_t n_offset, int fp16_logits, void* ws, size_t ws_bytes,
+                            cudaStream_t s, const P2PArgs* p2p, const void* x_param, const NormArgs* norm);
+int lm_head_argmax_impl(const void* x, const void* w, void* out_key, void* out_index, int64_t M, int64_t K,
+                        int64_t N, int64_t n_offset, int fp16_logits, void* ws, size_t ws_bytes, cudaStream_t s);
+const P2PArgs* p2p_args_checked(void* ctx, int64_t n_offset, int64_t N, int* status);
+
 // Device-side error bits: kernels OR one in when a bounded wait gives up.
 enum : unsigned { kDevErrTimeout = 1u };
 

@@ -30,6 +30,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "neighbours.cuh"
 #include "w8a8_quant.cuh"
 
 namespace mcv {
@@ -61,6 +62,7 @@ struct RowArgs {
     int64_t n_offset;
     P2PArgs p2p;
     const __half* w_scale;  // int8 lm_head: per-row weight scales [N] (w then holds int8 rows)
+    NormArgs norm;          // argmax: rms_norm of x in the prologue (norm.gamma null: x as given)
 };
 
 __device__ __forceinline__ void st_relaxed_sys(uint64_t* p, uint64_t v) {
@@ -225,9 +227,16 @@ __device__ __forceinline__ void rows_body(const RowArgs& a, const uint4* xsrc) {
     }
     pdl_trigger();
     pdl_wait();
-    for (int idx = threadIdx.x; idx < M * chunks; idx += kRowThreads)
-        xs[idx] = xsrc[idx];
-    __syncthreads();
+    if (a.norm.gamma != nullptr) {
+        // lm_head_greedy's rms_norm (language_model.cpp:423), recomputed by
+        // every block from the raw hidden rows: x is 2 KB per row, and the
+        // first weight rows are already in flight
+        rms_norm_rows_block<M>(reinterpret_cast<const __half*>(xsrc), reinterpret_cast<__half*>(xs), a.K, a.norm);
+    } else {
+        for (int idx = threadIdx.x; idx < M * chunks; idx += kRowThreads)
+            xs[idx] = xsrc[idx];
+        __syncthreads();
+    }
 
     uint64_t best[M];
 #pragma unroll
@@ -627,7 +636,8 @@ int check_rows(const void* x, const void* w, int64_t M, int64_t K, int64_t N) {
 // parameters, the rows are passed by value in the launch and x is not read.
 int lm_head_argmax_impl_p2p(const void* x, const void* w, void* out_key, void* out_index, int64_t M,
                             int64_t K, int64_t N, int64_t n_offset, int fp16_logits, void* ws,
-                            size_t ws_bytes, cudaStream_t s, const P2PArgs* p2p, const void* x_param) {
+                            size_t ws_bytes, cudaStream_t s, const P2PArgs* p2p, const void* x_param,
+                            const NormArgs* norm) {
     const bool by_param = x_param != nullptr && M * K <= kXParamChunks * 8;
     int st = check_rows(by_param ? w : x, w, M, K, N);
     if (st) return st;
@@ -648,6 +658,10 @@ int lm_head_argmax_impl_p2p(const void* x, const void* w, void* out_key, void* o
     a.K = static_cast<int>(K);
     a.n_offset = n_offset;
     if (p2p) a.p2p = *p2p;
+    if (norm && norm->gamma) {
+        if (norm->variant != 0 && norm->variant != 1) return fail(MCV_ERR_VALUE, "lm_head: norm variant must be 0 or 1");
+        a.norm = *norm;
+    }
     if (by_param) {
         RowArgsXP ax{};
         ax.a = a;
@@ -708,7 +722,7 @@ int lm_head_argmax_impl(const void* x, const void* w, void* out_key, void* out_i
                         int64_t K, int64_t N, int64_t n_offset, int fp16_logits, void* ws,
                         size_t ws_bytes, cudaStream_t s) {
     return lm_head_argmax_impl_p2p(x, w, out_key, out_index, M, K, N, n_offset, fp16_logits, ws, ws_bytes, s,
-                                   nullptr, nullptr);
+                                   nullptr, nullptr, nullptr);
 }
 
 int key_to_index_impl(const void* key, void* out_index, int64_t M, cudaStream_t s) {
@@ -780,6 +794,24 @@ int mcv_lm_head_argmax(const void* x, const void* w, void* out_key, void* out_in
     if (!out_key && !out_index) return fail(MCV_ERR_NULL, "lm_head_argmax: out_key and out_index both null");
     return lm_head_argmax_impl(x, w, out_key, out_index, M, K, N_shard, n_offset, fp16_logits, workspace,
                                workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int mcv_lm_head_argmax_rmsnorm(void* p2p_ctx, const void* x, const void* norm_gamma, float norm_eps,
+                               int norm_variant, const void* w, void* out_key, void* out_index, int64_t M,
+                               int64_t K, int64_t N_shard, int64_t n_offset, int fp16_logits, void* workspace,
+                               size_t workspace_bytes, mcv_stream_t stream) {
+    if (!out_key && !out_index) return fail(MCV_ERR_NULL, "lm_head_argmax_rmsnorm: out_key and out_index both null");
+    if (!norm_gamma) return fail(MCV_ERR_NULL, "lm_head_argmax_rmsnorm: null gamma");
+    if (norm_variant != 0 && norm_variant != 1) return fail(MCV_ERR_VALUE, "lm_head_argmax_rmsnorm: variant must be 0 or 1");
+    const P2PArgs* pa = nullptr;
+    if (p2p_ctx) {
+        int st = MCV_OK;
+        pa = p2p_args_checked(p2p_ctx, n_offset, N_shard, &st);
+        if (st) return st;
+    }
+    const NormArgs na{static_cast<const __half*>(norm_gamma), norm_eps, norm_variant};
+    return lm_head_argmax_impl_p2p(x, w, out_key, out_index, M, K, N_shard, n_offset, fp16_logits, workspace,
+                                   workspace_bytes, static_cast<cudaStream_t>(stream), pa, nullptr, &na);
 }
 
 int mcv_argmax_last_dim_f16(const void* logits, void* out_index, int64_t M, int64_t V, mcv_stream_t stream) {

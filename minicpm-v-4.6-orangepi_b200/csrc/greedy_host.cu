@@ -1,26 +1,23 @@
 // One greedy decoding step of the lm_head from host memory to a host token
-// id in one native call: the device half of the reference's lm_head_greedy
-// (src/csrc/lib/language_model.cpp:412-482), which hands the token back to
-// the host.  x rides in the launch parameters when small (else one copy-in),
+// id in one native call: the reference's lm_head_greedy
+// (src/csrc/lib/language_model.cpp:412-482) - final rms_norm, vocabulary
+// GEMV, first-max argmax - which hands the token back to the host.  x rides in the launch parameters when small (else one copy-in),
 // the fused GEMV + argmax stores the index straight into page-locked host
 // memory (else one 8-byte copy-out), then the stream is synchronised: one
 // library call and, for a 1024-wide row, one queued GPU operation per token.
 #include "common.cuh"
 
 namespace mcv {
-int lm_head_argmax_impl_p2p(const void* x, const void* w, void* out_key, void* out_index, int64_t M, int64_t K,
-                            int64_t N, int64_t n_offset, int fp16_logits, void* ws, size_t ws_bytes,
-                            cudaStream_t s, const P2PArgs* p2p, const void* x_param);
-const P2PArgs* p2p_args_checked(void* ctx, int64_t n_offset, int64_t N, int* status);
 }  // namespace mcv
 
 using namespace mcv;
 
 extern "C" {
 
-int mcv_lm_head_greedy_host(void* p2p_ctx, const void* x_host, void* x_dev, const void* w, void* index_dev,
-                            int64_t* index_host, int64_t M, int64_t K, int64_t N_shard, int64_t n_offset,
-                            int fp16_logits, void* workspace, size_t workspace_bytes, mcv_stream_t stream) {
+int mcv_lm_head_greedy_host(void* p2p_ctx, const void* x_host, void* x_dev, const void* norm_gamma, float norm_eps,
+                            const void* w, void* index_dev, int64_t* index_host, int64_t M, int64_t K,
+                            int64_t N_shard, int64_t n_offset, int fp16_logits, void* workspace,
+                            size_t workspace_bytes, mcv_stream_t stream) {
     if (!x_host || !x_dev || !index_dev || !index_host) return fail(MCV_ERR_NULL, "lm_head_greedy_host: null pointer");
     if (M < 1 || M > 8 || K < 1) return fail(MCV_ERR_SHAPE, "lm_head_greedy_host: M must be 1..8");
     // x_host is read on the host when it travels in the launch: refuse
@@ -33,6 +30,9 @@ int mcv_lm_head_greedy_host(void* p2p_ctx, const void* x_host, void* x_dev, cons
         (void)cudaGetLastError();  // unregistered host memory
     }
     auto s = static_cast<cudaStream_t>(stream);
+    // lm_head_greedy's final rms_norm (language_model.cpp:423), fused into
+    // the kernel's prologue when a gamma is given
+    const NormArgs norm{static_cast<const __half*>(norm_gamma), norm_eps, 0};
     const P2PArgs* pa = nullptr;
     if (p2p_ctx) {
         int st = MCV_OK;
@@ -57,7 +57,7 @@ int mcv_lm_head_greedy_host(void* p2p_ctx, const void* x_host, void* x_dev, cons
         (void)cudaGetLastError();  // pageable memory: not an error, copy out below
     const int st = lm_head_argmax_impl_p2p(by_param ? nullptr : x_dev, w, nullptr, out, M, K, N_shard, n_offset,
                                            fp16_logits, workspace, workspace_bytes, s, pa,
-                                           by_param ? x_host : nullptr);
+                                           by_param ? x_host : nullptr, norm_gamma ? &norm : nullptr);
     if (st) return st;
     cudaError_t e = cudaSuccess;
     if (out == index_dev) {

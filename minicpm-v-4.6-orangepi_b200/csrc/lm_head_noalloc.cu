@@ -13,9 +13,6 @@
 #include "common.cuh"
 
 namespace mcv {
-int lm_head_argmax_impl(const void* x, const void* w, void* out_key, void* out_index, int64_t M, int64_t K,
-                        int64_t N, int64_t n_offset, int fp16_logits, void* ws, size_t ws_bytes,
-                        cudaStream_t s);
 
 namespace {
 

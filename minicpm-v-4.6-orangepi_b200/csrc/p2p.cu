@@ -1,22 +1,21 @@
 // Vocab-sharded lm_head with the cross-GPU (max, index) reduction fused into
 // the kernel over NVLink peer memory, in place of a separate NCCL all-reduce.
 //
-// Every rank owns a small mailbox (2 KB) in its own HBM and maps every
-// peer's mailbox through CUDA IPC.  The last block of each rank's fused
-// lm_head + argmax kernel stores the rank's 64-bit keys into all mailboxes
-// with release stores, waits (bounded, 1 s) for all peers' keys in its own
-// mailbox, and writes the global winner - one kernel, no collective launch.
-// A per-rank call counter in device memory tags the keys, so captured CUDA
-// graphs replay correctly; slots alternate by counter parity.
+// Every rank owns a small mailbox (128 64-bit slots, 1 KB, plus a call
+// counter and an error word) in its own HBM and maps every peer's mailbox
+// through CUDA IPC.  The last block of each rank's fused lm_head + argmax
+// kernel writes the rank's keys into all mailboxes, one relaxed system-scope
+// 64-bit store per key and peer (the word carries the key and an 8-bit call
+// tag together, so no fence is needed), waits (bounded, 1 s) for all peers'
+// keys in its own mailbox, and writes the global winner - one kernel, no
+// collective launch.  The call counter lives in device memory, so captured
+// CUDA graphs replay correctly; slots alternate by counter parity.
 //
 // The reference has no multi-device code (it runs its 16 lm_head chunks one
 // after another on one NPU, src/csrc/lib/language_model.cpp:464-480).
 #include "common.cuh"
 
 namespace mcv {
-int lm_head_argmax_impl_p2p(const void* x, const void* w, void* out_key, void* out_index, int64_t M, int64_t K,
-                            int64_t N, int64_t n_offset, int fp16_logits, void* ws, size_t ws_bytes,
-                            cudaStream_t s, const P2PArgs* p2p, const void* x_param);
 
 namespace {
 
@@ -128,7 +127,8 @@ int mcv_lm_head_argmax_p2p(void* ctx, const void* x, const void* w, void* out_ke
     if (n_offset < 0 || N_shard < 0 || n_offset + N_shard > kP2PMaxIndex)
         return fail(MCV_ERR_SHAPE, "lm_head_argmax_p2p: vocabulary indices must stay below 2^24 - 1");
     return lm_head_argmax_impl_p2p(x, w, out_key, out_index, M, K, N_shard, n_offset, fp16_logits, workspace,
-                                   workspace_bytes, static_cast<cudaStream_t>(stream), &c->args, nullptr);
+                                   workspace_bytes, static_cast<cudaStream_t>(stream), &c->args, nullptr,
+                                   nullptr);
 }
 
 }  // extern "C"

@@ -41,6 +41,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "neighbours.cuh"
 
 namespace mcv {
 namespace {
@@ -454,6 +455,109 @@ w4a16_ksplit_kernel(const __grid_constant__ GroupParams gp) {
     }
 }
 
+int assign_strips(GroupParams& gp);
+
+// The K-split kernel for the down projection with silu_mul fused into its
+// activation load: x = silu(gate) * up (decoder_layer.cpp:1203-1204, the
+// silu_mul kernel's arithmetic in neighbours.cuh).  Each warp turns exactly
+// the activation slices of its own 128-k groups (M rows x 128) into a
+// warp-private shared-memory tile, all 32 lanes sharing the exp work, then
+// runs the same MMAs as w4a16_ksplit_kernel reading x from that tile.
+template <int M, int KG>
+__global__ void __launch_bounds__(kWarps * 32)
+w4a16_ksplit_silu_kernel(const __grid_constant__ GroupParams gp, const __half* __restrict__ up) {
+    __shared__ float4 red[kWarps][32];
+    extern __shared__ __align__(16) __half xsilu[];  // [warp][KG][M][128]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int strip = static_cast<int>(blockIdx.x);
+    const Problem& P = gp.p[0];
+    const int K = P.K, G = K / kGroup, Gp = (G + 7) & ~7, zw = (G + 7) >> 3;
+    const int col = strip * 16 + g;
+    uint4 v[KG][2];
+    float slo[KG], shi[KG];
+    int zlo[KG], zhi[KG];
+#pragma unroll
+    for (int j = 0; j < KG; ++j) {
+        const int gi = warp + j * kWarps;
+        v[j][0] = v[j][1] = make_uint4(0, 0, 0, 0);
+        slo[j] = shi[j] = 0.0f;
+        zlo[j] = zhi[j] = 0;
+        if (gi < G) {
+            const size_t base = (static_cast<size_t>(strip) * (K / 64) + 2 * gi) * 32 + lane;
+            v[j][0] = ld_stream(P.qw + base);
+            v[j][1] = ld_stream(P.qw + base + 32);
+            slo[j] = __half2float(P.s[static_cast<size_t>(col) * Gp + gi]);
+            shi[j] = __half2float(P.s[static_cast<size_t>(col + 8) * Gp + gi]);
+            zlo[j] = static_cast<int>((P.z[static_cast<size_t>(col) * zw + (gi >> 3)] >> (4 * (gi & 7))) & 0xfu);
+            zhi[j] = static_cast<int>((P.z[static_cast<size_t>(col + 8) * zw + (gi >> 3)] >> (4 * (gi & 7))) & 0xfu);
+        }
+    }
+    pdl_trigger();
+    pdl_wait();  // gate and up are the previous kernel's outputs
+    __half* xw = xsilu + static_cast<size_t>(warp) * KG * M * kGroup;
+#pragma unroll
+    for (int j = 0; j < KG; ++j) {
+        const int gi = warp + j * kWarps;
+        if (gi >= G) break;
+        for (int e = lane; e < M * (kGroup / 8); e += 32) {
+            const int m = e / (kGroup / 8), c = e % (kGroup / 8);
+            const size_t off = static_cast<size_t>(m) * K + gi * kGroup + c * 8;
+            const uint4 gv = *reinterpret_cast<const uint4*>(P.x + off);
+            const uint4 uv = *reinterpret_cast<const uint4*>(up + off);
+            *reinterpret_cast<uint4*>(xw + (j * M + m) * kGroup + c * 8) = silu_mul8(gv, uv);
+        }
+    }
+    __syncwarp();
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int j = 0; j < KG; ++j) {
+        const int gi = warp + j * kWarps;
+        if (gi >= G) break;
+        float d[4];
+        group_mma<M>(v[j], xw + (j * M + (g < M ? g : 0)) * kGroup + 16 * t, g, zlo[j] + P.zero_bias,
+                     zhi[j] + P.zero_bias, d);
+        acc[0] = fmaf(d[0], slo[j], acc[0]);
+        acc[1] = fmaf(d[1], slo[j], acc[1]);
+        acc[2] = fmaf(d[2], shi[j], acc[2]);
+        acc[3] = fmaf(d[3], shi[j], acc[3]);
+    }
+    red[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    __syncthreads();
+    if (warp == 0) {
+        float4 sum = red[0][lane];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) {
+            const float4 r = red[w][lane];
+            sum.x += r.x;
+            sum.y += r.y;
+            sum.z += r.z;
+            sum.w += r.w;
+        }
+        const float out4[4] = {sum.x, sum.y, sum.z, sum.w};
+        store_strip<M>(P, strip, lane, out4);
+    }
+}
+
+template <int M>
+int launch_silu_m(GroupParams& gp, const __half* up, cudaStream_t st) {
+    const int strips = assign_strips(gp);
+    const int G = gp.p[0].K / kGroup;
+    const int per_warp = (G + kWarps - 1) / kWarps;
+    auto go = [&](auto kern, int kg) -> int {
+        const size_t smem = static_cast<size_t>(kWarps) * kg * M * kGroup * 2;
+        if (smem > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a16_ksplit_silu)");
+        }
+        return launch(kern, dim3(strips), dim3(kWarps * 32), smem, st, gp, up);
+    };
+    if (per_warp <= 1) return go(w4a16_ksplit_silu_kernel<M, 1>, 1);
+    if (per_warp <= 2) return go(w4a16_ksplit_silu_kernel<M, 2>, 2);
+    if (per_warp <= 4) return go(w4a16_ksplit_silu_kernel<M, 4>, 4);
+    return go(w4a16_ksplit_silu_kernel<M, 8>, 8);
+}
+
 int assign_strips(GroupParams& gp) {
     int t = 0;
     for (int i = 0; i < gp.count; ++i) {
@@ -688,6 +792,37 @@ int mcv_w4a16_gemv(const void* x, const void* qweight, const void* scales, const
     mcv_w4a16_problem p{x, qweight, scales, zeros, out, static_cast<int32_t>(K), static_cast<int32_t>(N),
                         static_cast<int32_t>(group), zero_bias};
     return mcv_w4a16_gemv_grouped(&p, 1, M, stream);
+}
+
+int mcv_w4a16_gemv_silu_mul(const void* gate, const void* up, const void* qweight, const void* scales,
+                            const void* zeros, int zero_bias, void* out, int64_t M, int64_t K, int64_t N,
+                            int64_t group, mcv_stream_t stream) {
+    if (!gate || !up || !qweight || !scales || !zeros || !out) return fail(MCV_ERR_NULL, "w4a16_gemv_silu_mul: null pointer");
+    if (M < 1 || M > 8) return fail(MCV_ERR_SHAPE, "w4a16_gemv_silu_mul: M must be 1..8");
+    int st = check_layout_dims(K, N, group);
+    if (st) return st;
+    if (K > 8 * kWarps * kGroup) return fail(MCV_ERR_SHAPE, "w4a16_gemv_silu_mul: K above 8192 unsupported");
+    if (!aligned16(qweight) || !aligned16(scales) || !aligned16(gate) || !aligned16(up))
+        return fail(MCV_ERR_ALIGN, "w4a16_gemv_silu_mul: gate, up, qweight and scales must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(zeros) & 3u) return fail(MCV_ERR_ALIGN, "w4a16_gemv_silu_mul: zeros must be 4-byte aligned");
+    if (zero_bias < 0 || zero_bias > 1) return fail(MCV_ERR_VALUE, "w4a16_gemv_silu_mul: zero_bias must be 0 or 1");
+    GroupParams gp{};
+    gp.count = 1;
+    gp.p[0] = Problem{static_cast<const __half*>(gate), static_cast<const uint4*>(qweight),
+                      static_cast<const __half*>(scales), static_cast<const uint32_t*>(zeros), static_cast<__half*>(out),
+                      static_cast<int>(K), static_cast<int>(N), zero_bias, 0};
+    auto s = static_cast<cudaStream_t>(stream);
+    auto u = static_cast<const __half*>(up);
+    switch (M) {
+        case 1: return launch_silu_m<1>(gp, u, s);
+        case 2: return launch_silu_m<2>(gp, u, s);
+        case 3: return launch_silu_m<3>(gp, u, s);
+        case 4: return launch_silu_m<4>(gp, u, s);
+        case 5: return launch_silu_m<5>(gp, u, s);
+        case 6: return launch_silu_m<6>(gp, u, s);
+        case 7: return launch_silu_m<7>(gp, u, s);
+        default: return launch_silu_m<8>(gp, u, s);
+    }
 }
 
 int mcv_w4a16_gemv_grouped(const mcv_w4a16_problem* problems, int count, int64_t M, mcv_stream_t stream) {

@@ -29,6 +29,7 @@ _i64 = ctypes.c_int64
 _int = ctypes.c_int
 _vp = ctypes.c_void_p
 _sz = ctypes.c_size_t
+_f32 = ctypes.c_float
 
 # name -> argtypes (restype int unless listed in _RESTYPE)
 _SIGS = {
@@ -65,7 +66,12 @@ _SIGS = {
     "mcv_p2p_destroy": [_vp],
     "mcv_p2p_errors": [_vp],
     "mcv_lm_head_argmax_p2p": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _sz, _vp],
-    "mcv_lm_head_greedy_host": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _sz, _vp],
+    "mcv_lm_head_greedy_host": [_vp, _vp, _vp, _vp, _f32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _sz, _vp],
+    "mcv_lm_head_argmax_rmsnorm": [_vp, _vp, _vp, _f32, _int, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _sz,
+                                   _vp],
+    "mcv_rms_norm": [_vp, _vp, _vp, _i64, _i64, _f32, _int, _vp],
+    "mcv_silu_mul": [_vp, _vp, _vp, _i64, _vp],
+    "mcv_w4a16_gemv_silu_mul": [_vp, _vp, _vp, _vp, _vp, _int, _vp, _i64, _i64, _i64, _i64, _vp],
     "mcv_w8a8_quantize": [_vp, _vp, _vp, _i64, _i64, _vp],
     "mcv_w8a8_gemm_i32": [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
     "mcv_w8a8_dequant": [_vp, _vp, _vp, _vp, _i64, _i64, _vp],
@@ -259,6 +265,15 @@ def matmul_w4a16(x, w: W4A16QuantizedWeight, out, stream=None) -> None:
                                 M, w.K, w.N, w.group_size, _stream(stream)), "matmul_w4a16")
 
 
+def matmul_w4a16_silu_mul(gate, up, w: W4A16QuantizedWeight, out, stream=None) -> None:
+    """out fp16 [M,N] = (silu(gate) * up) @ dequant(w): the down projection
+    with silu_mul fused into its activation load (mcv_w4a16_gemv_silu_mul)."""
+    M = gate.shape[0] if gate.dim() == 2 else 1
+    _check(lib().mcv_w4a16_gemv_silu_mul(_ptr(gate), _ptr(up), _ptr(w.qweight), _ptr(w.scales), _ptr(w.zeros),
+                                         w.zero_bias, _ptr(out), M, w.K, w.N, w.group_size, _stream(stream)),
+           "matmul_w4a16_silu_mul")
+
+
 def matmul_w4a16_gemm(x, w: W4A16QuantizedWeight, out, stream=None) -> None:
     """out fp16 [M,N] = x fp16 [M,K] @ dequant(w) on the tcgen05 tensor cores (M >= 16)."""
     M = x.shape[0]
@@ -395,18 +410,47 @@ def lm_head_argmax_p2p(ctx: P2PContext, x, w_shard, workspace, out_key, out_inde
 # ---- W8A8 -----------------------------------------------------------------------
 
 def lm_head_greedy_host(x_host, x_dev, w_shard, index_dev, index_host, workspace, ctx: "P2PContext" = None,
-                        n_offset: int = 0, fp16_logits: bool = False, stream=None) -> None:
+                        n_offset: int = 0, fp16_logits: bool = False, norm_gamma=None, norm_eps: float = 1e-6,
+                        stream=None) -> None:
     """Host x (pinned fp16 [M,K]) -> host int64 [M] global argmax indices in
-    one call: copy in, fused lm_head + argmax (peer exchange when `ctx`),
-    copy out, stream sync (mcv_lm_head_greedy_host)."""
+    one call: copy in, (final rms_norm with `norm_gamma`,) fused lm_head +
+    argmax (peer exchange when `ctx`), copy out, stream sync
+    (mcv_lm_head_greedy_host)."""
     M, K = x_host.shape
     N = w_shard.shape[0]
     if x_host.is_cuda or index_host.is_cuda:
         raise RuntimeError("lm_head_greedy_host: x_host and index_host live in host memory")
     _check(lib().mcv_lm_head_greedy_host(ctx.handle if ctx is not None else None, _vp(x_host.data_ptr()), _ptr(x_dev),
-                                         _ptr(w_shard), _ptr(index_dev), _vp(index_host.data_ptr()), M, K, N, n_offset,
-                                         int(fp16_logits), _ptr(workspace), workspace.numel(), _stream(stream)),
+                                         _ptr(norm_gamma), norm_eps, _ptr(w_shard), _ptr(index_dev),
+                                         _vp(index_host.data_ptr()), M, K, N, n_offset, int(fp16_logits),
+                                         _ptr(workspace), workspace.numel(), _stream(stream)),
            "lm_head_greedy_host")
+
+
+def lm_head_argmax_rmsnorm(x, norm_gamma, w_shard, workspace, out_index=None, out_key=None, norm_eps: float = 1e-6,
+                           norm_variant: int = 0, ctx: "P2PContext" = None, n_offset: int = 0,
+                           fp16_logits: bool = False, stream=None) -> None:
+    """lm_head_greedy's device half with its final rms_norm fused in
+    (mcv_lm_head_argmax_rmsnorm): x is the raw last hidden state [M,K]."""
+    M, K = x.shape
+    _check(lib().mcv_lm_head_argmax_rmsnorm(ctx.handle if ctx is not None else None, _ptr(x), _ptr(norm_gamma),
+                                            norm_eps, norm_variant, _ptr(w_shard), _ptr(out_key), _ptr(out_index),
+                                            M, K, w_shard.shape[0], n_offset, int(fp16_logits), _ptr(workspace),
+                                            workspace.numel(), _stream(stream)),
+           "lm_head_argmax_rmsnorm")
+
+
+def rms_norm(x, gamma, out, eps: float = 1e-6, variant: int = 0, stream=None) -> None:
+    """out [rows,H] = rms_norm(x); variant 0 = the engine's rms_norm (fp16
+    chain, 1 + gamma), 1 = rms_norm1024's fp32 arithmetic (mcv_rms_norm)."""
+    H = x.shape[-1]
+    rows = x.numel() // H
+    _check(lib().mcv_rms_norm(_ptr(x), _ptr(gamma), _ptr(out), rows, H, eps, variant, _stream(stream)), "rms_norm")
+
+
+def silu_mul(gate, up, out, stream=None) -> None:
+    """out = silu(gate) * up (mcv_silu_mul)."""
+    _check(lib().mcv_silu_mul(_ptr(gate), _ptr(up), _ptr(out), gate.numel(), _stream(stream)), "silu_mul")
 
 
 class LmHeadGreedyStep:
@@ -415,18 +459,19 @@ class LmHeadGreedyStep:
     library call (pass `w_shard` to switch weights between calls)."""
 
     def __init__(self, x_host, x_dev, w_shard, index_dev, index_host, workspace, ctx: "P2PContext" = None,
-                 n_offset: int = 0, fp16_logits: bool = False, stream=None):
+                 n_offset: int = 0, fp16_logits: bool = False, norm_gamma=None, norm_eps: float = 1e-6, stream=None):
         if x_host.is_cuda or index_host.is_cuda:
             raise RuntimeError("LmHeadGreedyStep: x_host and index_host live in host memory")
         M, K = x_host.shape
         self._fn = lib().mcv_lm_head_greedy_host
         self._shape = (M, K)
         self._rows = w_shard.shape[0]
-        self._head = (ctx.handle if ctx is not None else None, _vp(x_host.data_ptr()), _ptr(x_dev))
+        self._head = (ctx.handle if ctx is not None else None, _vp(x_host.data_ptr()), _ptr(x_dev), _ptr(norm_gamma),
+                      norm_eps)
         self._w = _ptr(w_shard)
         self._tail = (_ptr(index_dev), _vp(index_host.data_ptr()), M, K)
         self._rest = (n_offset, int(fp16_logits), _ptr(workspace), workspace.numel(), _stream(stream))
-        self._keep = (x_host, x_dev, w_shard, index_dev, index_host, workspace)
+        self._keep = (x_host, x_dev, w_shard, index_dev, index_host, workspace, norm_gamma)
 
     def __call__(self, w_shard=None) -> None:
         w = self._w

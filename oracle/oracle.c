@@ -515,3 +515,48 @@ void orc_quantize_dense_weight_w8a8(const uint16_t* w_kn, int64_t K, int64_t N, 
         for (int64_t k = 0; k < K; ++k) wq[k * N + n] = quantize_i8(t[w_kn[k * N + n]], inv);
     }
 }
+
+/* ------------------------------------------------------------------------ */
+/* rms_norm (engine chain and the fp32 custom kernel) and silu_mul           */
+/* ------------------------------------------------------------------------ */
+
+static inline uint16_t rn16(float f) { return orc_f32_to_f16_rn(f); }
+
+void orc_rms_norm_chain(const uint16_t* x, const uint16_t* gamma, int64_t M, int64_t H, float eps,
+                        uint16_t* out) {
+    const float* t = h2f_table();
+    for (int64_t m = 0; m < M; ++m) {
+        const uint16_t* xr = x + m * H;
+        double sum = 0.0; /* exact: fp16 squares span < 53 bits */
+        for (int64_t h = 0; h < H; ++h) sum += (double)t[rn16(t[xr[h]] * t[xr[h]])];
+        const uint16_t mean = rn16((float)sum / (float)H);
+        const uint16_t ms = rn16(t[mean] + eps);
+        const uint16_t rstd = rn16(1.0f / sqrtf(t[ms]));
+        for (int64_t h = 0; h < H; ++h) {
+            const uint16_t scaled = rn16(t[xr[h]] * t[rstd]);
+            const uint16_t gp1 = rn16(t[gamma[h]] + 1.0f);
+            out[m * H + h] = rn16(t[scaled] * t[gp1]);
+        }
+    }
+}
+
+void orc_rms_norm_fp32(const uint16_t* x, const uint16_t* gamma, int64_t M, int64_t H, float eps,
+                       uint16_t* out) {
+    const float* t = h2f_table();
+    for (int64_t m = 0; m < M; ++m) {
+        const uint16_t* xr = x + m * H;
+        double sum = 0.0;
+        for (int64_t h = 0; h < H; ++h) sum += (double)t[xr[h]] * (double)t[xr[h]];
+        const float inv = 1.0f / sqrtf((float)sum * (1.0f / (float)H) + eps);
+        for (int64_t h = 0; h < H; ++h) out[m * H + h] = rn16((t[xr[h]] * inv) * t[gamma[h]]);
+    }
+}
+
+void orc_silu_mul(const uint16_t* gate, const uint16_t* up, int64_t n, uint16_t* out) {
+    const float* t = h2f_table();
+    for (int64_t i = 0; i < n; ++i) {
+        const float g = t[gate[i]];
+        const float s = g / (1.0f + expf(-g));
+        out[i] = rn16(s * t[up[i]]);
+    }
+}

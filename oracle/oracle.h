@@ -135,6 +135,27 @@ void orc_quantize_dense_weight_w8a8(const uint16_t* w_kn, int64_t K, int64_t N,
  * smaller index (the first-max rule above).  -0 is canonicalised to +0. */
 uint64_t orc_argmax_key(float logit, uint32_t index);
 
+
+/* ---- neighbours of the GEMVs: rms_norm and silu_mul -------------------- */
+/* The engine's rms_norm (src/csrc/lib/ops.cpp:564-737), which lm_head_greedy
+ * applies before the lm_head (src/csrc/lib/language_model.cpp:423) and every
+ * decoder layer before its projections: a chain of fp16 tensor ops, each
+ * result rounded to fp16 - x_sq = x*x; mean over the row; + eps; rsqrt;
+ * x * rstd; gamma + 1; (x * rstd) * (gamma + 1).  The mean's sum is taken
+ * exactly (a double sum of fp16 squares, which no order changes) and then
+ * rounded through fp32 to fp16: the reference's aclnnMean leaves the
+ * accumulation order unspecified. */
+void orc_rms_norm_chain(const uint16_t* x, const uint16_t* gamma, int64_t M, int64_t H, float eps,
+                        uint16_t* out);
+/* The rms_norm1024 custom kernel (op_kernel/rms_norm1024_custom.cpp:57-70):
+ * fp32 throughout, inv = 1 / sqrt(sum(x^2) / H + eps), out = RN(x * inv * gamma)
+ * (gamma itself, no +1); the sum of squares is taken in double. */
+void orc_rms_norm_fp32(const uint16_t* x, const uint16_t* gamma, int64_t M, int64_t H, float eps,
+                       uint16_t* out);
+/* silu_mul (op_kernel/silu_mul_custom.cpp:63-72): fp32
+ * s = g / (1 + exp(-g)), out = RN(s * u). */
+void orc_silu_mul(const uint16_t* gate, const uint16_t* up, int64_t n, uint16_t* out);
+
 #ifdef __cplusplus
 }
 #endif

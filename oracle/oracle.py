@@ -265,3 +265,31 @@ def quantize_dense_weight_w8a8(w_kn):
     ws = np.empty(N, np.uint16)
     lib().orc_quantize_dense_weight_w8a8(_ptr(w), _i64(K), _i64(N), _ptr(wq), _ptr(ws))
     return wq, ws
+
+
+# ---- rms_norm / silu_mul --------------------------------------------------------
+
+def rms_norm(x, gamma, eps: float = 1e-6, variant: int = 0) -> np.ndarray:
+    """fp16 bits [M,H].  variant 0: the engine's fp16 op chain with (1 + gamma)
+    (src/csrc/lib/ops.cpp:564-737); 1: the fp32 rms_norm1024 custom kernel
+    with gamma (op_kernel/rms_norm1024_custom.cpp:57-70)."""
+    x = _u16(x)
+    if x.ndim == 1:
+        x = x[None, :]
+    g = _u16(gamma).reshape(-1)
+    M, H = x.shape
+    assert g.size == H
+    out = np.empty((M, H), np.uint16)
+    fn = lib().orc_rms_norm_chain if variant == 0 else lib().orc_rms_norm_fp32
+    fn(_ptr(x), _ptr(g), _i64(M), _i64(H), ctypes.c_float(eps), _ptr(out))
+    return out
+
+
+def silu_mul(gate, up) -> np.ndarray:
+    """fp16 bits, shape of gate; op_kernel/silu_mul_custom.cpp:63-72."""
+    g = _u16(gate)
+    u = _u16(up)
+    assert g.shape == u.shape
+    out = np.empty(g.shape, np.uint16)
+    lib().orc_silu_mul(_ptr(g), _ptr(u), _i64(g.size), _ptr(out))
+    return out

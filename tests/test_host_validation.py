@@ -66,8 +66,27 @@ def test_lm_head_arguments(L):
 def test_lm_head_greedy_host_arguments(L):
     g = L.mcv_lm_head_greedy_host
     ws_bytes = L.mcv_lm_head_workspace_size(1)
-    assert g(None, None, F, F, F, F, 1, 1024, 1000, 0, 0, F, ws_bytes, None) == NULL
-    assert g(None, F, F, F, F, F, 9, 1024, 1000, 0, 0, F, ws_bytes, None) == SHAPE
+    assert g(None, None, F, None, 1e-6, F, F, F, 1, 1024, 1000, 0, 0, F, ws_bytes, None) == NULL
+    assert g(None, F, F, None, 1e-6, F, F, F, 9, 1024, 1000, 0, 0, F, ws_bytes, None) == SHAPE
+
+
+def test_neighbour_arguments(L):
+    ws_bytes = L.mcv_lm_head_workspace_size(1)
+    r = L.mcv_lm_head_argmax_rmsnorm
+    assert r(None, F, None, 1e-6, 0, F, None, F, 1, 1024, 1000, 0, 0, F, ws_bytes, None) == NULL   # gamma
+    assert r(None, F, F, 1e-6, 2, F, None, F, 1, 1024, 1000, 0, 0, F, ws_bytes, None) == VALUE    # variant
+    assert r(None, F, F, 1e-6, 0, F, None, None, 1, 1024, 1000, 0, 0, F, ws_bytes, None) == NULL  # outputs
+    assert L.mcv_rms_norm(F, None, F, 1, 1024, 1e-6, 0, None) == NULL
+    assert L.mcv_rms_norm(F, F, F, 1, 1024, 1e-6, 3, None) == VALUE
+    assert L.mcv_rms_norm(F, F, F, 0, 1024, 1e-6, 0, None) == SHAPE
+    assert L.mcv_silu_mul(F, F, None, 8, None) == NULL
+    assert L.mcv_silu_mul(F2, F, F, 8, None) == ALIGN
+    assert L.mcv_silu_mul(F, F, F, 0, None) == SHAPE
+    s = L.mcv_w4a16_gemv_silu_mul
+    assert s(F, F, F, F, F, 0, F, 9, 1024, 3584, 128, None) == SHAPE      # M
+    assert s(F, F, F, F, F, 0, F, 1, 16384, 3584, 128, None) == SHAPE     # K above 8192
+    assert s(F, None, F, F, F, 0, F, 1, 1024, 3584, 128, None) == NULL
+    assert s(F2, F, F, F, F, 0, F, 1, 1024, 3584, 128, None) == ALIGN
 
 
 def test_w8a8_arguments(L):
