@@ -46,7 +46,8 @@ enum mcv_status {
     MCV_ERR_NCCL = 5,        /* an NCCL call failed */
     MCV_ERR_WORKSPACE = 6,   /* workspace missing or too small */
     MCV_ERR_VALUE = 7,       /* bad argument value (layout code, g_idx, zero range) */
-    MCV_ERR_TIMEOUT = 8      /* a bounded device-side wait gave up */
+    MCV_ERR_TIMEOUT = 8,     /* a bounded device-side wait gave up */
+    MCV_ERR_FORMAT = 9       /* a file cannot be read or is not a valid safetensors file */
 };
 
 const char* mcv_status_string(int status);
@@ -72,13 +73,17 @@ void mcv_set_pdl(int enabled);
  *   slices fit the SMs and every slice keeps >= 4 stages of 64 k.
  *   MCV_TUNE_W8A8_KERNEL: the [N][K] W8A8 kernel - 1 = DP4A dot products,
  *   2 = integer tensor-core MMAs (mma.sync m16n8k32 s8); default: DP4A for
- *   M = 1, MMAs from M = 2.  Both give the same bits. */
+ *   M = 1, MMAs from M = 2.  Both give the same bits.
+ *   MCV_TUNE_W4A16_GRID: blocks of the bulk-copy streaming W4A16 kernel
+ *   (capped at 3 per SM); default: the fewest blocks that keep the largest
+ *   per-warp strip count, so every warp owns the same number of strips. */
 enum mcv_tuning_key {
     MCV_TUNE_W4A16_MODE = 2,
     MCV_TUNE_ROWS_BLOCKS_PER_SM = 3,
     MCV_TUNE_ROWS_PREFETCH = 4,
     MCV_TUNE_GEMM_SPLIT_K = 5,
     MCV_TUNE_W8A8_KERNEL = 6,
+    MCV_TUNE_W4A16_GRID = 7,
     MCV_TUNE_COUNT = 8
 };
 int mcv_set_tuning(int key, int value);
@@ -400,6 +405,48 @@ int mcv_lm_head_argmax_w8a8(const void* x, const void* w_int8, const void* w_sca
  * Replaces quantize_dense_weight_w8a8 (src/csrc/lib/quantized_weight.cpp:231-268). */
 int mcv_w8a8_quantize_weight(const void* w_kn, void* wq, void* w_scale, int64_t K, int64_t N,
                              int w_layout, mcv_stream_t stream);
+
+/* ======================================================================== */
+/* Checkpoints: safetensors reader and the GPTQ / AWQ loader                  */
+/* ======================================================================== */
+
+/* Element types of safetensors tensors. */
+enum mcv_dtype {
+    MCV_DT_F16 = 1, MCV_DT_BF16 = 2, MCV_DT_F32 = 3, MCV_DT_F64 = 4, MCV_DT_I8 = 5,
+    MCV_DT_U8 = 6, MCV_DT_I16 = 7, MCV_DT_I32 = 8, MCV_DT_I64 = 9, MCV_DT_BOOL = 10
+};
+/* Opens and memory-maps a .safetensors file and parses its header (replaces
+ * WeightsIndex, src/csrc/lib/weights.cpp:197-333): every tensor's byte range is
+ * checked against its dtype, shape and the file size (MCV_ERR_FORMAT
+ * otherwise).  Close with mcv_safetensors_close. */
+int mcv_safetensors_open(const char* path, void** st_out);
+int mcv_safetensors_close(void* st);
+/* Number of tensors and their names in sorted order (WeightsIndex::names). */
+int64_t mcv_safetensors_count(const void* st);
+const char* mcv_safetensors_name(const void* st, int64_t i);
+/* dtype (mcv_dtype), rank (<= 8), shape, host address of the data inside the
+ * mapping (valid until close) and byte size; any output may be NULL. */
+int mcv_safetensors_info(const void* st, const char* name, int* dtype, int* rank, int64_t* shape,
+                         const void** data, uint64_t* nbytes);
+/* Copies an F16 tensor, or a BF16 one converted to F16 by the reference's
+ * truncating rule (load_to_device_as, weights.cpp:25-33, 239-262), to device
+ * memory (dst_bytes >= the tensor's 2-byte-per-element size). */
+int mcv_safetensors_copy_f16(const void* st, const char* name, void* dst_dev, uint64_t dst_bytes,
+                             mcv_stream_t stream);
+/* Dimensions of the quantized projection `base` (base.qweight / .qzeros /
+ * .scales, plus .g_idx for GPTQ; without .g_idx it is AWQ), with the dtype and
+ * shape checks of quantized_weight.cpp:75-160.  Use K and N with
+ * mcv_w4a16_layout_bytes to size the device buffers. */
+int mcv_w4a16_safetensors_dims(const void* st, const char* base, int64_t* K, int64_t* N, int* is_gptq);
+/* load_w4a16_quantized_weight (src/csrc/lib/quantized_weight.cpp:212-229):
+ * the checkpoint's GPTQ or AWQ tensors repacked into the mcv-int4 arrays in
+ * the caller's device buffers (scales may be F16 or BF16); *zero_bias_out as
+ * the pack_*_host functions set it.  Synchronous (the host staging is
+ * released on return).  The _host form writes host arrays instead. */
+int mcv_w4a16_load_safetensors(const void* st, const char* base, void* qweight_dev, void* scales_dev,
+                               void* zeros_dev, int* zero_bias_out, mcv_stream_t stream);
+int mcv_w4a16_load_safetensors_host(const void* st, const char* base, uint32_t* qweight, uint16_t* scales,
+                                    uint32_t* zeros, int* zero_bias_out);
 
 /* ======================================================================== */
 /* The GEMVs' element-wise neighbours                                        */

@@ -64,6 +64,7 @@ const char* mcv_status_string(int status) {
         case MCV_ERR_WORKSPACE: return "workspace missing or too small";
         case MCV_ERR_VALUE: return "bad argument value";
         case MCV_ERR_TIMEOUT: return "device wait timed out";
+        case MCV_ERR_FORMAT: return "unreadable or malformed file";
         default: return "unknown status";
     }
 }

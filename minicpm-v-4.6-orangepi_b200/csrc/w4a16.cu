@@ -595,7 +595,17 @@ int launch_m(GroupParams& gp, cudaStream_t st) {
     auto kern = w4a16_tma_kernel<M>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTmaSmem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a16_tma)");
-    const int blocks = std::min((strips + kWarps - 1) / kWarps, sm_count() * kTmaBlocksPerSm);
+    // Each warp owns whole strips (strip, strip + W, ...), so the launch
+    // lasts as long as the warps with the most strips.  Use the fewest warps
+    // that keep that maximum: every warp then has the same count (e.g. 48
+    // config-0 GEMVs = 10752 strips: 2688 warps with 4 strips each, instead of
+    // 3552 warps of which 96 take a 4th strip while the rest idle).
+    const int max_blocks = sm_count() * kTmaBlocksPerSm;
+    const int per_warp = (strips + max_blocks * kWarps - 1) / (max_blocks * kWarps);
+    const int warps = (strips + per_warp - 1) / per_warp;
+    int blocks = std::min((warps + kWarps - 1) / kWarps, max_blocks);
+    const int t = tuning(MCV_TUNE_W4A16_GRID);
+    if (t > 0) blocks = std::min(t, max_blocks);
     return launch(kern, dim3(blocks), dim3(kWarps * 32), static_cast<size_t>(kTmaSmem), st, gp);
 }
 

@@ -71,6 +71,15 @@ _SIGS = {
                                    _vp],
     "mcv_rms_norm": [_vp, _vp, _vp, _i64, _i64, _f32, _int, _vp],
     "mcv_silu_mul": [_vp, _vp, _vp, _i64, _vp],
+    "mcv_safetensors_open": [ctypes.c_char_p, _vp],
+    "mcv_safetensors_close": [_vp],
+    "mcv_safetensors_count": [_vp],
+    "mcv_safetensors_name": [_vp, _i64],
+    "mcv_safetensors_info": [_vp, ctypes.c_char_p, _vp, _vp, _vp, _vp, _vp],
+    "mcv_safetensors_copy_f16": [_vp, ctypes.c_char_p, _vp, ctypes.c_uint64, _vp],
+    "mcv_w4a16_safetensors_dims": [_vp, ctypes.c_char_p, _vp, _vp, _vp],
+    "mcv_w4a16_load_safetensors": [_vp, ctypes.c_char_p, _vp, _vp, _vp, _vp, _vp],
+    "mcv_w4a16_load_safetensors_host": [_vp, ctypes.c_char_p, _vp, _vp, _vp, _vp],
     "mcv_w4a16_gemv_silu_mul": [_vp, _vp, _vp, _vp, _vp, _int, _vp, _i64, _i64, _i64, _i64, _vp],
     "mcv_w8a8_quantize": [_vp, _vp, _vp, _i64, _i64, _vp],
     "mcv_w8a8_gemm_i32": [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
@@ -95,6 +104,8 @@ _RESTYPE = {
     "mcv_p2p_handle_bytes": _sz,
     "mcv_p2p_errors": ctypes.c_uint,
     "mcv_lm_head_noalloc_max_bytes": _sz,
+    "mcv_safetensors_count": _i64,
+    "mcv_safetensors_name": ctypes.c_char_p,
 }
 EXPORTED = tuple(_SIGS)
 
@@ -256,6 +267,115 @@ def pack_w4a16_from_tiles(packed: np.ndarray, scales_gn: np.ndarray, K: int, N: 
     _check(lib().mcv_w4a16_pack_from_tiles_host(_ptr(p), p.shape[1], _ptr(s), K, N, _ptr(qw), _ptr(sc),
                                                 _ptr(zw), ctypes.byref(zb)), "pack_w4a16_from_tiles")
     return _to_device(qw, sc, zw, zb.value, K, N, 128, device)
+
+
+# ---- checkpoints (safetensors) ---------------------------------------------------
+
+_NP_DTYPE = {1: np.float16, 2: np.uint16, 3: np.float32, 4: np.float64, 5: np.int8, 6: np.uint8, 7: np.int16,
+             8: np.int32, 9: np.int64, 10: np.bool_}
+DTYPE_NAMES = {1: "F16", 2: "BF16", 3: "F32", 4: "F64", 5: "I8", 6: "U8", 7: "I16", 8: "I32", 9: "I64", 10: "BOOL"}
+
+
+class SafeTensors:
+    """A memory-mapped .safetensors file (mcv_safetensors_open): the
+    counterpart of the reference's WeightsIndex (weights.cpp:197-333)."""
+
+    def __init__(self, path: str):
+        self.handle = _vp()
+        _check(lib().mcv_safetensors_open(os.fsencode(path), ctypes.byref(self.handle)), "safetensors_open")
+
+    def close(self) -> None:
+        if self.handle:
+            lib().mcv_safetensors_close(self.handle)
+            self.handle = _vp()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def names(self):
+        L = lib()
+        return [L.mcv_safetensors_name(self.handle, i).decode() for i in range(L.mcv_safetensors_count(self.handle))]
+
+    def __contains__(self, name: str) -> bool:
+        return name in set(self.names())
+
+    def info(self, name: str):
+        """(dtype name, shape tuple, nbytes)."""
+        dt, rank, nb = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_uint64(0)
+        shape = (ctypes.c_int64 * 8)()
+        _check(lib().mcv_safetensors_info(self.handle, name.encode(), ctypes.byref(dt), ctypes.byref(rank), shape,
+                                          None, ctypes.byref(nb)), "safetensors_info")
+        return DTYPE_NAMES[dt.value], tuple(shape[i] for i in range(rank.value)), nb.value
+
+    def numpy(self, name: str) -> np.ndarray:
+        """A copy of the tensor's elements (BF16 as raw uint16 bits)."""
+        dt, rank, nb = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_uint64(0)
+        shape = (ctypes.c_int64 * 8)()
+        data = _vp()
+        _check(lib().mcv_safetensors_info(self.handle, name.encode(), ctypes.byref(dt), ctypes.byref(rank), shape,
+                                          ctypes.byref(data), ctypes.byref(nb)), "safetensors_info")
+        raw = ctypes.string_at(data, nb.value) if nb.value else b""
+        return np.frombuffer(raw, dtype=_NP_DTYPE[dt.value]).reshape([shape[i] for i in range(rank.value)]).copy()
+
+    def to_device_f16(self, name: str, device="cuda"):
+        """An F16 (or BF16, converted as the reference's loader does) tensor on the device."""
+        import torch
+        _, shape, nb = self.info(name)
+        elems = int(np.prod(shape)) if shape else 1
+        t = torch.empty(shape, dtype=torch.float16, device=device)
+        _check(lib().mcv_safetensors_copy_f16(self.handle, name.encode(), _ptr(t), elems * 2, None),
+               "safetensors_copy_f16")
+        torch.cuda.synchronize(device)
+        return t
+
+
+def has_w4a16_quantized_weight(st: SafeTensors, base: str) -> bool:
+    """quantized_weight.cpp:204-210."""
+    names = set(st.names())
+    return all(base + sfx in names for sfx in (".qweight", ".qzeros", ".scales"))
+
+
+def _safetensors_dims(st: SafeTensors, base: str):
+    K, N, g = ctypes.c_int64(0), ctypes.c_int64(0), ctypes.c_int(0)
+    _check(lib().mcv_w4a16_safetensors_dims(st.handle, base.encode(), ctypes.byref(K), ctypes.byref(N),
+                                            ctypes.byref(g)), "w4a16_safetensors_dims")
+    return K.value, N.value, bool(g.value)
+
+
+def load_w4a16_quantized_weight_host(st: SafeTensors, base: str):
+    """(qweight, scales, zeros, zero_bias, K, N) of the mcv-int4 layout as host arrays."""
+    K, N, _ = _safetensors_dims(st, base)
+    qw, sc, zw = _alloc_layout_host(K, N, 128)
+    zb = ctypes.c_int(0)
+    _check(lib().mcv_w4a16_load_safetensors_host(st.handle, base.encode(), _ptr(qw), _ptr(sc), _ptr(zw),
+                                                 ctypes.byref(zb)), "w4a16_load_safetensors_host")
+    return qw, sc, zw, zb.value, K, N
+
+
+def load_w4a16_quantized_weight(st: SafeTensors, base: str, device="cuda") -> W4A16QuantizedWeight:
+    """load_w4a16_quantized_weight (quantized_weight.cpp:212-229): the
+    checkpoint's GPTQ or AWQ projection `base` in the mcv-int4 layout on the
+    device (mcv_w4a16_load_safetensors)."""
+    import torch
+    K, N, _ = _safetensors_dims(st, base)
+    G = K // 128
+    Np, Gp = (N + 15) // 16 * 16, (G + 7) // 8 * 8
+    qw = torch.empty(Np * K // 8, dtype=torch.int32, device=device)
+    sc = torch.empty((Np, Gp), dtype=torch.float16, device=device)
+    zw = torch.empty((Np, (G + 7) // 8), dtype=torch.int32, device=device)
+    zb = ctypes.c_int(0)
+    _check(lib().mcv_w4a16_load_safetensors(st.handle, base.encode(), _ptr(qw), _ptr(sc), _ptr(zw), ctypes.byref(zb),
+                                            None), "w4a16_load_safetensors")
+    return W4A16QuantizedWeight(qw, sc, zw, zb.value, K, N, 128)
 
 
 def matmul_w4a16(x, w: W4A16QuantizedWeight, out, stream=None) -> None:

@@ -45,3 +45,25 @@ def cuda():
     import mcv_b200
     mcv_b200.lib()
     return torch
+
+
+def write_safetensors(path, tensors, metadata=None, header_pad=0):
+    """Writes a .safetensors file: 8-byte little-endian header length, the
+    JSON header {name: {dtype, shape, data_offsets}} (+ __metadata__), then the
+    tensors' bytes in order.  tensors: {name: (dtype string, numpy array)}."""
+    import json
+    import struct
+    header, blobs, off = {}, [], 0
+    if metadata is not None:
+        header["__metadata__"] = metadata
+    for name, (dt, arr) in tensors.items():
+        b = np.ascontiguousarray(arr).tobytes()
+        header[name] = {"dtype": dt, "shape": list(arr.shape), "data_offsets": [off, off + len(b)]}
+        blobs.append(b)
+        off += len(b)
+    h = json.dumps(header).encode() + b" " * header_pad
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(h)))
+        f.write(h)
+        for b in blobs:
+            f.write(b)
