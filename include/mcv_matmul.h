@@ -128,6 +128,13 @@ int mcv_w4a16_pack_host(const uint8_t* q_kn, const uint8_t* z_gn, const uint16_t
                         int64_t K, int64_t N, int64_t group, uint32_t* qweight_out,
                         uint16_t* scales_out, uint32_t* zeros_out);
 
+/* The inverse of the packers: the mcv-int4 arrays back to the logical
+ * (q - zero) int8 [K][N] and scales fp16 [K/group][N] - the form the
+ * reference's unpackers produce (HostW4A16Weight, quantized_weight.cpp:19-25).
+ * For checking a loaded checkpoint against another loader. */
+int mcv_w4a16_unpack_host(const uint32_t* qweight, const uint16_t* scales, const uint32_t* zeros, int zero_bias,
+                          int64_t K, int64_t N, int64_t group, int8_t* w_kn, uint16_t* scales_gn);
+
 /* Host repack of a GPTQ checkpoint tensor set (qweight int32 [K/8][N],
  * qzeros int32 [G][N/8], g_idx int32 [K] or NULL, scales fp16 [G][N]).
  * Replaces unpack_gptq_weight + pack_w4a16_weight of

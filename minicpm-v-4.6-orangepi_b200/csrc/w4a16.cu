@@ -699,6 +699,36 @@ int mcv_w4a16_pack_host(const uint8_t* q_kn, const uint8_t* z_gn, const uint16_t
     return MCV_OK;
 }
 
+int mcv_w4a16_unpack_host(const uint32_t* qw, const uint16_t* sc, const uint32_t* zw, int zero_bias, int64_t K,
+                          int64_t N, int64_t group, int8_t* w_kn, uint16_t* scales_gn) {
+    if (!qw || !sc || !zw || !w_kn || !scales_gn) return fail(MCV_ERR_NULL, "w4a16_unpack_host: null pointer");
+    int st = check_layout_dims(K, N, group);
+    if (st) return st;
+    const int64_t G = K / group, Gp = padded_g(G), KQ = K / 64, zwords = (G + 7) / 8;
+    // inverse of pack_layout: nibble slot kFragSlot[e] of word j of lane
+    // vector (strip, kq, lane) holds (n, k) = (16 strip + g + kFragRow[e],
+    // 64 kq + 16 t + 4 j + kFragK[e])
+    for (int64_t strip = 0; strip < padded_n(N) / 16; ++strip)
+        for (int64_t kq = 0; kq < KQ; ++kq)
+            for (int lane = 0; lane < 32; ++lane)
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t word = qw[((strip * KQ + kq) * 32 + lane) * 4 + j];
+                    const int gg = lane >> 2, t = lane & 3;
+                    for (int e = 0; e < 8; ++e) {
+                        const int64_t n = strip * 16 + gg + kFragRow[e];
+                        const int64_t k = kq * 64 + 16 * t + 4 * j + kFragK[e];
+                        if (n >= N) continue;
+                        const int q = static_cast<int>((word >> (4 * kFragSlot[e])) & 0xfu);
+                        const int z = static_cast<int>((zw[n * zwords + (k / group) / 8] >> (4 * ((k / group) % 8))) & 0xfu) +
+                                      zero_bias;
+                        w_kn[k * N + n] = static_cast<int8_t>(q - z);
+                    }
+                }
+    for (int64_t g = 0; g < G; ++g)
+        for (int64_t n = 0; n < N; ++n) scales_gn[g * N + n] = sc[n * Gp + g];
+    return MCV_OK;
+}
+
 int mcv_w4a16_pack_gptq_host(const int32_t* qweight, const int32_t* qzeros, const int32_t* g_idx,
                              const uint16_t* scales, int64_t K, int64_t N, int64_t group,
                              uint32_t* qw, uint16_t* sc, uint32_t* zw, int* zero_bias_out) {

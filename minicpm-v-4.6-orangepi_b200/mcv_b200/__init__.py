@@ -42,6 +42,7 @@ _SIGS = {
     "mcv_device_errors": [],
     "mcv_w4a16_layout_bytes": [_i64, _i64, _i64, _vp, _vp, _vp],
     "mcv_w4a16_pack_host": [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp],
+    "mcv_w4a16_unpack_host": [_vp, _vp, _vp, _int, _i64, _i64, _i64, _vp, _vp],
     "mcv_w4a16_pack_gptq_host": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp],
     "mcv_w4a16_pack_awq_host": [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp],
     "mcv_w4a16_pack_from_tiles_host": [_vp, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _vp],
@@ -349,6 +350,15 @@ def _safetensors_dims(st: SafeTensors, base: str):
     _check(lib().mcv_w4a16_safetensors_dims(st.handle, base.encode(), ctypes.byref(K), ctypes.byref(N),
                                             ctypes.byref(g)), "w4a16_safetensors_dims")
     return K.value, N.value, bool(g.value)
+
+
+def unpack_w4a16_host(qw, sc, zw, zero_bias: int, K: int, N: int, group: int = 128):
+    """mcv-int4 host arrays -> ((q - zero) int8 [K,N], scales fp16 bits [G,N])."""
+    w = np.empty((K, N), np.int8)
+    s = np.empty((K // group, N), np.uint16)
+    _check(lib().mcv_w4a16_unpack_host(_ptr(qw), _ptr(sc), _ptr(zw), zero_bias, K, N, group, _ptr(w), _ptr(s)),
+           "w4a16_unpack_host")
+    return w, s
 
 
 def load_w4a16_quantized_weight_host(st: SafeTensors, base: str):

@@ -265,6 +265,29 @@ void orc_w4a16_pack_tiles(const int8_t* w_kn, int64_t K, int64_t N, int64_t tile
         }
 }
 
+void orc_w4a16_unpack_tiles(const int8_t* packed, int64_t K, int64_t N, int64_t tile_len, int8_t* w_kn) {
+    const int64_t G = 128, groups = K / G;
+    const int64_t block_len = (N + 7) / 8;
+    const int64_t tpb = (block_len + tile_len - 1) / tile_len;
+    for (int64_t g = 0; g < groups; ++g)
+        for (int64_t b = 0; b < 8; ++b) {
+            const int64_t bstart = b * block_len;
+            int64_t bvalid = N - bstart;
+            if (bvalid > block_len) bvalid = block_len;
+            if (bvalid < 0) bvalid = 0;
+            for (int64_t t = 0; t < tpb; ++t) {
+                const int64_t tstart = t * tile_len;
+                int64_t tvalid = bvalid - tstart;
+                if (tvalid > tile_len) tvalid = tile_len;
+                if (tvalid < 0) tvalid = 0;
+                const int64_t base = (((g * 8 + b) * tpb + t) * G) * tile_len;
+                for (int64_t kk = 0; kk < G; ++kk)
+                    for (int64_t i = 0; i < tvalid; ++i)
+                        w_kn[(g * G + kk) * N + bstart + tstart + i] = packed[base + kk * tile_len + i];
+            }
+        }
+}
+
 /* ------------------------------------------------------------------------ */
 /* dense fp16 GEMV and the lm_head argmax                                     */
 /* ------------------------------------------------------------------------ */

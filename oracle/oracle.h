@@ -80,6 +80,8 @@ int64_t orc_w4a16_choose_tile_len(int64_t N);
 int64_t orc_w4a16_tile_rows(int64_t K, int64_t N, int64_t tile_len);
 void orc_w4a16_pack_tiles(const int8_t* w_kn, int64_t K, int64_t N, int64_t tile_len,
                           int8_t* packed);
+/* The inverse: tile-packed [rows][tile_len] back to w [K,N]. */
+void orc_w4a16_unpack_tiles(const int8_t* packed, int64_t K, int64_t N, int64_t tile_len, int8_t* w_kn);
 
 /* ---- dense fp16 GEMV / lm_head ----------------------------------------- */
 /* out[m,n] = fp32 sum over ascending k of x[m,k]*w(k,n); w_layout 0 = [N,K]
