@@ -75,8 +75,12 @@ void mcv_set_pdl(int enabled);
  *   2 = integer tensor-core MMAs (mma.sync m16n8k32 s8); default: DP4A for
  *   M = 1, MMAs from M = 2.  Both give the same bits.
  *   MCV_TUNE_W4A16_GRID: blocks of the bulk-copy streaming W4A16 kernel
- *   (capped at 3 per SM); default: the fewest blocks that keep the largest
- *   per-warp strip count, so every warp owns the same number of strips. */
+ *   (capped at 3 per SM); default: 3 per SM, or one warp per strip when
+ *   there are fewer strips.
+ *   MCV_TUNE_W4A16_MATH: the W4A16 GEMV's per-group arithmetic - 1 = exact
+ *   (q - zero) per weight on four MMA chains, 2 = the same on two chains with
+ *   integer-built zero constants, 3 = zero point folded out (raw
+ *   exponent-bias weights, sum(x) from an all-ones MMA). */
 enum mcv_tuning_key {
     MCV_TUNE_W4A16_MODE = 2,
     MCV_TUNE_ROWS_BLOCKS_PER_SM = 3,
@@ -84,7 +88,8 @@ enum mcv_tuning_key {
     MCV_TUNE_GEMM_SPLIT_K = 5,
     MCV_TUNE_W8A8_KERNEL = 6,
     MCV_TUNE_W4A16_GRID = 7,
-    MCV_TUNE_COUNT = 8
+    MCV_TUNE_W4A16_MATH = 8,
+    MCV_TUNE_COUNT = 10
 };
 int mcv_set_tuning(int key, int value);
 /* Device-side error bits recorded since the last call (and cleared by it):
@@ -229,6 +234,18 @@ int mcv_w4a16_gemv_silu_mul(const void* gate, const void* up, const void* qweigh
  * ops.h:19) and the cube kernel op_kernel/matmul_cube_custom.cpp. */
 int mcv_gemv_f16(const void* x, const void* w, void* out, int64_t M, int64_t K, int64_t N,
                  int w_layout, mcv_stream_t stream);
+
+/* out fp16 [M][N] = x fp16 [M][K] . W^T, W fp16 [N][K], fp32 accumulation, on
+ * the tcgen05 tensor cores (TMA-fed shared-memory operands, accumulator in
+ * tensor memory; k split over a thread-block cluster when the output tiles
+ * leave SMs idle).  Any M >= 1 (meant for M > 8, where the GEMV stops);
+ * K a multiple of 64, N a multiple of 8.  Replaces matmul_b_transposed's
+ * aclnnMm / K-tiled path for M > 1 (src/csrc/lib/ops.cpp:215-322). */
+int mcv_gemm_f16(const void* x, const void* w, void* out, int64_t M, int64_t K, int64_t N, mcv_stream_t stream);
+/* dst fp16 [cols][rows] = src fp16 [rows][cols]^T: the load-time transpose that
+ * turns the reference's pre-transposed [K][N] weights (load_matmul_weight_transposed,
+ * src/csrc/lib/language_model.cpp:84-105) back into [N][K] for mcv_gemm_f16. */
+int mcv_transpose_f16(const void* src, void* dst, int64_t rows, int64_t cols, mcv_stream_t stream);
 
 /* Workspace bytes for mcv_lm_head_argmax with M rows; must be zero-filled
  * once before first use (each call leaves it zeroed again). */

@@ -85,7 +85,8 @@ void matmul_w4a16(const T& x, const W4A16Weight& w, T& out, cudaStream_t stream,
 }
 
 /* out [M,N] = a [M,K] . B with b stored [N,K] or [K,N], told apart by a's K
- * as the reference does (ops.cpp:165-171); M = 1..8.  ops.h:19. */
+ * as the reference does (ops.cpp:165-171): the GEMV for M <= 8, the
+ * tensor-core GEMM beyond ([N,K] weights only).  ops.h:19. */
 template <class T>
 void matmul_b_transposed(const T& a, const T& b, T& out, cudaStream_t stream, bool sync = false) {
     detail::need_rank2(a, "matmul_b_transposed");
@@ -100,7 +101,13 @@ void matmul_b_transposed(const T& a, const T& b, T& out, cudaStream_t stream, bo
     } else {
         throw Error(MCV_ERR_SHAPE, "matmul_b_transposed: K dim mismatch");
     }
-    check(mcv_gemv_f16(a.data(), b.data(), out.data(), M, K, N, layout, stream), "matmul_b_transposed");
+    if (M > 8) {
+        // the tensor-core GEMM takes [N,K]; a [K,N] weight needs mcv_transpose_f16 once at load time
+        if (layout != 0) throw Error(MCV_ERR_SHAPE, "matmul_b_transposed: M > 8 needs the weight as [N,K]");
+        check(mcv_gemm_f16(a.data(), b.data(), out.data(), M, K, N, stream), "matmul_b_transposed");
+    } else {
+        check(mcv_gemv_f16(a.data(), b.data(), out.data(), M, K, N, layout, stream), "matmul_b_transposed");
+    }
     finish(stream, sync, "matmul_b_transposed");
 }
 

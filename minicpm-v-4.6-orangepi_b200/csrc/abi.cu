@@ -10,6 +10,7 @@ namespace mcv {
 unsigned take_w4a16_device_error();
 unsigned take_dense_device_error();
 unsigned take_gemm_device_error();
+unsigned take_dense_gemm_device_error();
 
 namespace {
 thread_local std::string g_last_error;
@@ -85,7 +86,8 @@ int mcv_get_tuning(int key) { return mcv::tuning(key); }
 
 unsigned mcv_device_errors(void) {
     cudaDeviceSynchronize();
-    return mcv::take_w4a16_device_error() | mcv::take_dense_device_error() | mcv::take_gemm_device_error();
+    return mcv::take_w4a16_device_error() | mcv::take_dense_device_error() | mcv::take_gemm_device_error() |
+           mcv::take_dense_gemm_device_error();
 }
 
 }  // extern "C"

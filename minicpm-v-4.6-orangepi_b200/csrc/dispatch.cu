@@ -112,9 +112,13 @@ int mcv_matmul_decode_dispatch(const void* x, const mcv_decode_weights* w, void*
                               stream);
     }
     if (!w->dense) return fail(MCV_ERR_NULL, "matmul_decode_dispatch: no weight usable for this call");
-    // decoder_layer.cpp:243: the dense fp16 weight
-    if (M > 8) return fail(MCV_ERR_SHAPE, "matmul_decode_dispatch: the dense path takes M <= 8");
-    return mcv_gemv_f16(x, w->dense, out, M, K, N, w->dense_layout, stream);
+    // decoder_layer.cpp:243: the dense fp16 weight - GEMV up to 8 rows, the
+    // tensor-core GEMM beyond (which takes the [N][K] layout)
+    if (M <= 8) return mcv_gemv_f16(x, w->dense, out, M, K, N, w->dense_layout, stream);
+    if (w->dense_layout != 0)
+        return fail(MCV_ERR_SHAPE, "matmul_decode_dispatch: M > 8 on a dense weight needs the [N][K] layout "
+                                   "(mcv_transpose_f16 at load time)");
+    return mcv_gemm_f16(x, w->dense, out, M, K, N, stream);
 }
 
 }  // extern "C"

@@ -77,6 +77,18 @@ __device__ __forceinline__ void mma_16816(float d[4], const uint32_t a[4], uint3
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// fp16 bit patterns of the zero-point constants, built with integer ops
+// (no int -> fp16 conversion): 1024 + z (z < 1024) is 0x6400 | z, and
+// -(64 + z) for z < 64 is 0xD400 | (z << 4) (exponent 6, mantissa 16 z).
+__device__ __forceinline__ uint32_t h2_bits_1024_plus(int z) { return (0x6400u | static_cast<uint32_t>(z)) * 0x10001u; }
+__device__ __forceinline__ uint32_t h2_bits_neg_64_plus(int z) {
+    return (0xD400u | (static_cast<uint32_t>(z) << 4)) * 0x10001u;
+}
+
+template <int M, int MATH>
+__device__ __forceinline__ void group_mma(const uint4 (&v)[2], const __half* xg, int g, int zl_q, int zh_q,
+                                          float d[4]);
+
 // One 128-k group for one lane: v[0], v[1] are the lane's weight vectors of
 // the group's two quads, xg points at x[row g][group start + 16t] (read only
 // when g < M).  Dequantises and runs 8 MMAs on four independent accumulator
@@ -84,6 +96,80 @@ __device__ __forceinline__ void mma_16816(float d[4], const uint32_t a[4], uint3
 template <int M>
 __device__ __forceinline__ void group_mma(const uint4 (&v)[2], const __half* xg, int g, int zl_q, int zh_q,
                                           float d[4]) {
+    group_mma<M, 0>(v, xg, g, zl_q, zh_q, d);
+}
+
+template <int M, int MATH>
+__device__ __forceinline__ void group_mma(const uint4 (&v)[2], const __half* xg, int g, int zl_q, int zh_q,
+                                          float d[4]) {
+  if constexpr (MATH == 1 || MATH == 2) {
+    uint4 xv[2][2];
+#pragma unroll
+    for (int qd = 0; qd < 2; ++qd) {
+        xv[qd][0] = xv[qd][1] = make_uint4(0, 0, 0, 0);
+        if (g < M) {
+            xv[qd][0] = *reinterpret_cast<const uint4*>(xg + qd * 64);
+            xv[qd][1] = *reinterpret_cast<const uint4*>(xg + qd * 64 + 8);
+        }
+    }
+    constexpr uint32_t kMagic = 0x64006400u;
+    float c[2][4] = {};
+    float ones_acc[4] = {};
+    if constexpr (MATH == 1) {
+        // exact (q - zero) in fp16 per weight, two accumulator chains
+        const __half2 zl = u32_as_h2(h2_bits_1024_plus(zl_q)), zh = u32_as_h2(h2_bits_neg_64_plus(zh_q));
+        const __half2 inv16 = u32_as_h2(0x2c002c00u);
+#pragma unroll
+        for (int kb = 0; kb < 8; ++kb) {
+            const int qd = kb >> 2, j = kb & 3;
+            const uint4 vv = v[qd];
+            const uint32_t w = j == 0 ? vv.x : j == 1 ? vv.y : j == 2 ? vv.z : vv.w;
+            const uint4 xx = xv[qd][j >> 1];
+            const uint32_t b0 = (j & 1) ? xx.z : xx.x;
+            const uint32_t b1 = (j & 1) ? xx.w : xx.y;
+            const uint32_t w8 = w >> 8;
+            uint32_t a[4];
+            a[0] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w, 0x000f000fu, kMagic)), zl));
+            a[1] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w, 0x00f000f0u, kMagic)), inv16, zh));
+            a[2] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w8, 0x000f000fu, kMagic)), zl));
+            a[3] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w8, 0x00f000f0u, kMagic)), inv16, zh));
+            mma_16816(c[kb & 1], a, b0, b1);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) d[i] = c[0][i] + c[1][i];
+    } else {
+        // Zero point folded out of the per-weight work: the MMAs take the raw
+        // exponent-bias values (1024 + q for rows g, 1024 + 16 q for rows g+8,
+        // both exact in fp16) and a second MMA chain with an all-ones A
+        // operand gives S = sum(x) over the group in every row; then
+        //   sum x (q - z) = D_lo - (1024 + z) S = D_hi / 16 - (64 + z) S.
+        // Four instructions per 8 weights instead of eight.
+        const uint32_t ones[4] = {0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u};
+#pragma unroll
+        for (int kb = 0; kb < 8; ++kb) {
+            const int qd = kb >> 2, j = kb & 3;
+            const uint4 vv = v[qd];
+            const uint32_t w = j == 0 ? vv.x : j == 1 ? vv.y : j == 2 ? vv.z : vv.w;
+            const uint4 xx = xv[qd][j >> 1];
+            const uint32_t b0 = (j & 1) ? xx.z : xx.x;
+            const uint32_t b1 = (j & 1) ? xx.w : xx.y;
+            const uint32_t w8 = w >> 8;
+            uint32_t a[4];
+            a[0] = lop3_and_or(w, 0x000f000fu, kMagic);
+            a[1] = lop3_and_or(w, 0x00f000f0u, kMagic);
+            a[2] = lop3_and_or(w8, 0x000f000fu, kMagic);
+            a[3] = lop3_and_or(w8, 0x00f000f0u, kMagic);
+            mma_16816(c[kb & 1], a, b0, b1);
+            mma_16816(ones_acc, ones, b0, b1);
+        }
+        const float S0 = ones_acc[0], S1 = ones_acc[1];  // columns 2t, 2t+1 (every row holds them)
+        const float zl = -static_cast<float>(1024 + zl_q), zh = -static_cast<float>(64 + zh_q);
+        d[0] = fmaf(zl, S0, c[0][0] + c[1][0]);
+        d[1] = fmaf(zl, S1, c[0][1] + c[1][1]);
+        d[2] = fmaf(c[0][2] + c[1][2], 0.0625f, zh * S0);
+        d[3] = fmaf(c[0][3] + c[1][3], 0.0625f, zh * S1);
+    }
+  } else {
     uint4 xv[2][2];
 #pragma unroll
     for (int qd = 0; qd < 2; ++qd) {
@@ -117,6 +203,7 @@ __device__ __forceinline__ void group_mma(const uint4 (&v)[2], const __half* xg,
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) d[i] = (c[0][i] + c[1][i]) + (c[2][i] + c[3][i]);
+  }
 }
 
 struct Problem {
@@ -313,7 +400,7 @@ __device__ __forceinline__ void issue_item(const GroupParams& gp, const ItemIter
     cp_async_mbar_arrive(bar);
 }
 
-template <int M>
+template <int M, int MATH>
 __global__ void __launch_bounds__(kWarps * 32, kTmaBlocksPerSm)
 w4a16_tma_kernel(const __grid_constant__ GroupParams gp) {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -361,7 +448,7 @@ w4a16_tma_kernel(const __grid_constant__ GroupParams gp) {
             const uint4 v[2] = {*reinterpret_cast<const uint4*>(st + (2 * gi * 32 + lane) * 16),
                                 *reinterpret_cast<const uint4*>(st + ((2 * gi + 1) * 32 + lane) * 16)};
             float d[4];
-            group_mma<M>(v, xrow + gi * kGroup, g, static_cast<int>((zlo >> (4 * gi)) & 0xfu) + P.zero_bias,
+            group_mma<M, MATH>(v, xrow + gi * kGroup, g, static_cast<int>((zlo >> (4 * gi)) & 0xfu) + P.zero_bias,
                          static_cast<int>((zhi >> (4 * gi)) & 0xfu) + P.zero_bias, d);
             const float s_lo = half_of(slo, gi), s_hi = half_of(shi, gi);
             acc[0] = fmaf(d[0], s_lo, acc[0]);
@@ -392,7 +479,7 @@ w4a16_tma_kernel(const __grid_constant__ GroupParams gp) {
 // griddepcontrol.wait, and meet in shared memory for the final sum.  This
 // keeps a lone GEMV's critical path to one load latency plus 1/8 of its math.
 // ---------------------------------------------------------------------------
-template <int M, int KG>
+template <int M, int KG, int MATH>
 __global__ void __launch_bounds__(kWarps * 32)
 w4a16_ksplit_kernel(const __grid_constant__ GroupParams gp) {
     __shared__ float4 red[kWarps][32];
@@ -431,7 +518,7 @@ w4a16_ksplit_kernel(const __grid_constant__ GroupParams gp) {
         const int gi = warp + j * kWarps;
         if (gi >= G) break;
         float d[4];
-        group_mma<M>(v[j], P.x + static_cast<size_t>(g) * K + gi * kGroup + 16 * t, g, zlo[j] + P.zero_bias,
+        group_mma<M, MATH>(v[j], P.x + static_cast<size_t>(g) * K + gi * kGroup + 16 * t, g, zlo[j] + P.zero_bias,
                      zhi[j] + P.zero_bias, d);
         acc[0] = fmaf(d[0], slo[j], acc[0]);
         acc[1] = fmaf(d[1], slo[j], acc[1]);
@@ -568,7 +655,7 @@ int assign_strips(GroupParams& gp) {
     return t;
 }
 
-template <int M>
+template <int M, int MATH>
 int launch_m(GroupParams& gp, cudaStream_t st) {
     const int strips = assign_strips(gp);
     const int mode = tuning(MCV_TUNE_W4A16_MODE);
@@ -581,10 +668,10 @@ int launch_m(GroupParams& gp, cudaStream_t st) {
         for (int i = 0; i < gp.count; ++i) maxG = std::max(maxG, gp.p[i].K / kGroup);
         const int per_warp = (maxG + kWarps - 1) / kWarps;
         auto go = [&](auto kern) { return launch(kern, dim3(strips), dim3(kWarps * 32), 0, st, gp); };
-        if (per_warp <= 1) return go(w4a16_ksplit_kernel<M, 1>);
-        if (per_warp <= 2) return go(w4a16_ksplit_kernel<M, 2>);
-        if (per_warp <= 4) return go(w4a16_ksplit_kernel<M, 4>);
-        if (per_warp <= 8) return go(w4a16_ksplit_kernel<M, 8>);
+        if (per_warp <= 1) return go(w4a16_ksplit_kernel<M, 1, MATH>);
+        if (per_warp <= 2) return go(w4a16_ksplit_kernel<M, 2, MATH>);
+        if (per_warp <= 4) return go(w4a16_ksplit_kernel<M, 4, MATH>);
+        if (per_warp <= 8) return go(w4a16_ksplit_kernel<M, 8, MATH>);
         // larger K: the streaming kernel has no K limit
     }
     if (mode == 1) {
@@ -592,33 +679,40 @@ int launch_m(GroupParams& gp, cudaStream_t st) {
         const int blocks = std::min(strips, sm_count() * kBlocksPerSm);
         return launch(w4a16_gemv_kernel<M>, dim3(blocks), dim3(kWarps * 32), 0, st, gp);
     }
-    auto kern = w4a16_tma_kernel<M>;
+    auto kern = w4a16_tma_kernel<M, MATH>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTmaSmem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a16_tma)");
-    // Each warp owns whole strips (strip, strip + W, ...), so the launch
-    // lasts as long as the warps with the most strips.  Use the fewest warps
-    // that keep that maximum: every warp then has the same count (e.g. 48
-    // config-0 GEMVs = 10752 strips: 2688 warps with 4 strips each, instead of
-    // 3552 warps of which 96 take a 4th strip while the rest idle).
+    // As many warps as fit (3 blocks of 8 per SM): the stream is bound by
+    // bytes in flight per warp, so fewer warps with an even strip count each
+    // measured slower (48 config-0 GEMVs: 0.66 us per GEMV on 336 blocks
+    // against 0.55 us on 444, although 96 of the 3552 warps take a 4th strip).
     const int max_blocks = sm_count() * kTmaBlocksPerSm;
-    const int per_warp = (strips + max_blocks * kWarps - 1) / (max_blocks * kWarps);
-    const int warps = (strips + per_warp - 1) / per_warp;
-    int blocks = std::min((warps + kWarps - 1) / kWarps, max_blocks);
+    int blocks = std::min((strips + kWarps - 1) / kWarps, max_blocks);
     const int t = tuning(MCV_TUNE_W4A16_GRID);
     if (t > 0) blocks = std::min(t, max_blocks);
     return launch(kern, dim3(blocks), dim3(kWarps * 32), static_cast<size_t>(kTmaSmem), st, gp);
 }
 
-int run_group(GroupParams& gp, int64_t M, cudaStream_t st) {
+template <int MATH>
+int run_group_math(GroupParams& gp, int64_t M, cudaStream_t st) {
     switch (M) {
-        case 1: return launch_m<1>(gp, st);
-        case 2: return launch_m<2>(gp, st);
-        case 3: return launch_m<3>(gp, st);
-        case 4: return launch_m<4>(gp, st);
-        case 5: return launch_m<5>(gp, st);
-        case 6: return launch_m<6>(gp, st);
-        case 7: return launch_m<7>(gp, st);
-        default: return launch_m<8>(gp, st);
+        case 1: return launch_m<1, MATH>(gp, st);
+        case 2: return launch_m<2, MATH>(gp, st);
+        case 3: return launch_m<3, MATH>(gp, st);
+        case 4: return launch_m<4, MATH>(gp, st);
+        case 5: return launch_m<5, MATH>(gp, st);
+        case 6: return launch_m<6, MATH>(gp, st);
+        case 7: return launch_m<7, MATH>(gp, st);
+        default: return launch_m<8, MATH>(gp, st);
+    }
+}
+
+int run_group(GroupParams& gp, int64_t M, cudaStream_t st) {
+    switch (tuning(MCV_TUNE_W4A16_MATH)) {
+        case 1: return run_group_math<0>(gp, M, st);
+        case 2: return run_group_math<1>(gp, M, st);
+        case 3: return run_group_math<2>(gp, M, st);
+        default: return run_group_math<0>(gp, M, st);
     }
 }
 

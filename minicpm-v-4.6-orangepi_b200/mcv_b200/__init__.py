@@ -49,6 +49,8 @@ _SIGS = {
     "mcv_w4a16_gemv": [_vp, _vp, _vp, _vp, _int, _vp, _i64, _i64, _i64, _i64, _vp],
     "mcv_w4a16_gemv_grouped": [_vp, _int, _i64, _vp],
     "mcv_w4a16_gemm": [_vp, _vp, _vp, _vp, _int, _vp, _i64, _i64, _i64, _i64, _vp],
+    "mcv_gemm_f16": [_vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "mcv_transpose_f16": [_vp, _vp, _i64, _i64, _vp],
     "mcv_gemv_f16": [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
     "mcv_lm_head_workspace_size": [_i64],
     "mcv_lm_head_argmax": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _sz, _vp],
@@ -167,6 +169,8 @@ TUNE_ROWS_BLOCKS_PER_SM = 3
 TUNE_ROWS_PREFETCH = 4
 TUNE_GEMM_SPLIT_K = 5
 TUNE_W8A8_KERNEL = 6
+TUNE_W4A16_GRID = 7
+TUNE_W4A16_MATH = 8
 
 
 def device_errors() -> int:
@@ -439,7 +443,8 @@ def matmul_w4a16_grouped(items, M: int = 1, stream=None, problems=None) -> None:
 
 def matmul_b_transposed(a, b, out, stream=None) -> None:
     """out [M,N] = a [M,K] @ B with b stored [N,K] or [K,N], as the reference
-    disambiguates them (src/csrc/lib/ops.cpp:165-171); M = 1..8."""
+    disambiguates them (src/csrc/lib/ops.cpp:165-171): the GEMV for M <= 8,
+    the tensor-core GEMM beyond."""
     M, K = a.shape
     if b.shape[1] == K:
         layout, N = 0, b.shape[0]
@@ -449,7 +454,27 @@ def matmul_b_transposed(a, b, out, stream=None) -> None:
         raise RuntimeError("matmul_b_transposed K dim mismatch")
     if tuple(out.shape) != (M, N):
         raise RuntimeError("matmul_b_transposed out shape mismatch")
+    if M > 8:
+        # the tensor-core GEMM (mcv_gemm_f16) takes [N,K]; a [K,N] weight must
+        # be transposed once at load time (transpose_f16), as the caller owns memory
+        if layout != 0:
+            raise RuntimeError("matmul_b_transposed: M > 8 needs the weight as [N,K] (see transpose_f16)")
+        _check(lib().mcv_gemm_f16(_ptr(a), _ptr(b), _ptr(out), M, K, N, _stream(stream)), "matmul_b_transposed")
+        return
     _check(lib().mcv_gemv_f16(_ptr(a), _ptr(b), _ptr(out), M, K, N, layout, _stream(stream)), "matmul_b_transposed")
+
+
+def gemm_f16(x, w_nk, out, stream=None) -> None:
+    """out fp16 [M,N] = x fp16 [M,K] @ w_nk^T on the tcgen05 tensor cores (mcv_gemm_f16)."""
+    M, K = x.shape
+    N = w_nk.shape[0]
+    _check(lib().mcv_gemm_f16(_ptr(x), _ptr(w_nk), _ptr(out), M, K, N, _stream(stream)), "gemm_f16")
+
+
+def transpose_f16(src, dst, stream=None) -> None:
+    """dst [C,R] = src [R,C]^T (fp16), e.g. a [K,N] weight to the GEMM's [N,K]."""
+    R, C = src.shape
+    _check(lib().mcv_transpose_f16(_ptr(src), _ptr(dst), R, C, _stream(stream)), "transpose_f16")
 
 
 def lm_head_workspace(M: int = 1, device="cuda"):

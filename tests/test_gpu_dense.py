@@ -220,7 +220,7 @@ def test_lm_head_greedy_host_refuses_device_x(cuda):
     ws = mcv.lm_head_workspace(1)
     idx = torch.empty(1, dtype=torch.int64, device="cuda")
     host_idx = torch.empty(1, dtype=torch.int64).pin_memory()
-    st = L.mcv_lm_head_greedy_host(None, ctypes.c_void_p(xd.data_ptr()), ctypes.c_void_p(xd.data_ptr()),
+    st = L.mcv_lm_head_greedy_host(None, ctypes.c_void_p(xd.data_ptr()), ctypes.c_void_p(xd.data_ptr()), None, 1e-6,
                                    ctypes.c_void_p(w.data_ptr()), ctypes.c_void_p(idx.data_ptr()),
                                    ctypes.c_void_p(host_idx.data_ptr()), 1, 1024, 64, 0, 0,
                                    ctypes.c_void_p(ws.data_ptr()), ws.numel(), None)

@@ -158,3 +158,22 @@ def test_dp4a_and_tensor_core_kernels_same_bits(cuda, M):
     assert np.array_equal(got[1][0], got[2][0])
     _, r8 = oracle.w8a8_fused(x, w8, ws8)
     assert np.array_equal(got[2][0], r8)
+
+
+def test_gpu_weight_quantizer_equals_reference_code_output(cuda):
+    """The GPU quantizer against the reference's own quantize_dense_weight_w8a8
+    (src/csrc/lib/quantized_weight.cpp:231-268), run on the CPU by
+    tests/golden/make_ref_fixtures.py: int8 weights and fp16 scales bit-exact,
+    including a zero column and a column with a 65000 outlier."""
+    import make_ref_fixtures as reffix
+    import mcv_b200 as mcv
+    torch = cuda
+    w = reffix.w8a8_quant_input()
+    ref_wq, ref_ws = reffix.load_w8a8_quant()
+    K, N = w.shape
+    wq = torch.empty((K, N), dtype=torch.int8, device="cuda")
+    ws = torch.empty(N, dtype=torch.float16, device="cuda")
+    mcv.quantize_dense_weight_w8a8(torch.from_numpy(w).cuda(), wq, ws, w_layout=1)
+    torch.cuda.synchronize()
+    assert np.array_equal(wq.cpu().numpy(), ref_wq)
+    assert np.array_equal(ws.cpu().numpy().view(np.uint16), ref_ws)

@@ -108,7 +108,19 @@ def test_decode_dispatch_arguments(L):
     assert d(F, ctypes.byref(none), F, 1, 1024, 1024, None) == NULL        # no usable format
     dense = mcv_b200.DecodeWeights()
     dense.dense = 256
-    assert d(F, ctypes.byref(dense), F, 9, 1024, 1024, None) == SHAPE      # dense path is M <= 8
+    dense.dense_layout = 1
+    assert d(F, ctypes.byref(dense), F, 9, 1024, 1024, None) == SHAPE      # M > 8 on dense needs [N][K]
+
+
+def test_gemm_f16_arguments(L):
+    g = L.mcv_gemm_f16
+    assert g(None, F, F, 64, 1024, 4096, None) == NULL
+    assert g(F, F, F, 64, 1000, 4096, None) == SHAPE      # K % 64
+    assert g(F, F, F, 64, 1024, 4092, None) == SHAPE      # N % 8
+    assert g(F, F, F, 0, 1024, 4096, None) == SHAPE       # M
+    assert g(F2, F, F, 64, 1024, 4096, None) == ALIGN
+    assert L.mcv_transpose_f16(F, None, 4, 4, None) == NULL
+    assert L.mcv_transpose_f16(F, F, 0, 4, None) == SHAPE
 
 
 def test_context_set_up_arguments(L):
