@@ -260,13 +260,57 @@ def bench_w4a16_gemm(torch, mcv, synth, l2, hbm, tflops):
         copies = max(2, int(np.ceil(2 * l2 / w0.nbytes)))
         ws = [w0] + [mcv.W4A16QuantizedWeight(w0.qweight.clone(), w0.scales.clone(), w0.zeros.clone(), 0, K, N)
                      for _ in range(copies - 1)]
-        for M in (16, 64, 256, 1024):
+        for M in (16, 32, 64, 256, 1024):
+            x = torch.randn((M, K), device="cuda").to(torch.float16)
+            out = torch.empty((M, N), dtype=torch.float16, device="cuda")
+            flops = 2.0 * M * N * K
+            byts = synth.w4a16_bytes(M, K, N)
+            t_roof = max(byts / (hbm * 1e3), flops / (tflops * 1e6))  # us
+            entry = {"M": M, "N": N, "roofline_us": round(t_roof, 3)}
+            # the tcgen05 GEMM itself, and the public matmul_w4a16 (which
+            # serves M <= 32 on the widened GEMV)
+            for path, fn in (("tcgen05", mcv.matmul_w4a16_gemm), ("dispatched", mcv.matmul_w4a16)):
+                if path == "dispatched" and M > 32:
+                    continue
+
+                def step():
+                    for w in ws:
+                        fn(x, w, out)
+                step()
+                torch.cuda.synchronize()
+                g = graph_of(torch, step, torch.cuda.Stream())
+                g.replay()
+                torch.cuda.synchronize()
+                us = time_graph_ms(torch, g, reps=5) / copies * 1e3
+                r = {"us": round(us, 3), "TFLOPs": round(flops / (us * 1e-6) / 1e12, 2),
+                     "GBps": round(byts / (us * 1e-6) / 1e9, 1), "frac_of_roofline": round(t_roof / us, 4)}
+                if path == "tcgen05":
+                    entry.update(r)
+                else:
+                    entry["dispatched"] = dict(r, kernel="w4a16 GEMV, M <= 32")
+                del g
+            res.append(entry)
+        del ws
+    return {"config": "config4 W4A16 GEMM, tcgen05.mma kind::f16, fp32 accumulation in TMEM, K=1024", "cases": res}
+
+
+def bench_gemm_f16(torch, mcv, l2, hbm, tflops):
+    """The dense fp16 GEMM of matmul_b_transposed for M > 8 (tcgen05, both
+    operands TMA-staged): M in {16, 256, 1024}, K in {1024, 4096}, N = 4096;
+    weight copies rotate past 2x L2."""
+    res = []
+    N = 4096
+    for K in (1024, 4096):
+        w0 = (torch.randn((N, K), device="cuda") * 0.02).to(torch.float16)
+        copies = max(2, int(np.ceil(2 * l2 / (w0.numel() * 2))))
+        ws = [w0] + [w0.clone() for _ in range(copies - 1)]
+        for M in (16, 256, 1024):
             x = torch.randn((M, K), device="cuda").to(torch.float16)
             out = torch.empty((M, N), dtype=torch.float16, device="cuda")
 
             def step():
                 for w in ws:
-                    mcv.matmul_w4a16_gemm(x, w, out)
+                    mcv.gemm_f16(x, w, out)
             step()
             torch.cuda.synchronize()
             g = graph_of(torch, step, torch.cuda.Stream())
@@ -274,14 +318,15 @@ def bench_w4a16_gemm(torch, mcv, synth, l2, hbm, tflops):
             torch.cuda.synchronize()
             us = time_graph_ms(torch, g, reps=5) / copies * 1e3
             flops = 2.0 * M * N * K
-            byts = synth.w4a16_bytes(M, K, N)
-            t_roof = max(byts / (hbm * 1e3), flops / (tflops * 1e6))  # us
-            res.append({"M": M, "N": N, "us": round(us, 3), "TFLOPs": round(flops / (us * 1e-6) / 1e12, 2),
+            byts = N * K * 2 + M * K * 2 + M * N * 2
+            t_roof = max(byts / (hbm * 1e3), flops / (tflops * 1e6))
+            res.append({"M": M, "K": K, "N": N, "us": round(us, 3), "TFLOPs": round(flops / (us * 1e-6) / 1e12, 2),
                         "GBps": round(byts / (us * 1e-6) / 1e9, 1), "roofline_us": round(t_roof, 3),
                         "frac_of_roofline": round(t_roof / us, 4)})
             del g
         del ws
-    return {"config": "config4 W4A16 GEMM, tcgen05.mma kind::f16, fp32 accumulation in TMEM, K=1024", "cases": res}
+    return {"config": "dense fp16 GEMM (matmul_b_transposed, M > 8), tcgen05.mma kind::f16, fp32 accumulation",
+            "cases": res}
 
 
 def bench_lm_head_w8a8(torch, mcv, hbm, lm_w):
@@ -318,7 +363,11 @@ def bench_decode_step(torch, mcv, synth, hbm, lm_w, ws_lm):
     """Config 3: the 186 projections of one token + the lm_head.  'separate'
     launches each projection on its own (the reference's call pattern);
     'grouped' launches the projections that read the same input together
-    (qkv/z/a/b, q/k/v, gate/up): 96 W4A16 launches per token."""
+    (qkv/z/a/b, q/k/v, gate/up): 96 W4A16 launches per token.  The two
+    '+neighbours' variants add what sits between the matmuls on the hot
+    path - silu_mul between each layer's gate/up and down projections and the
+    final rms_norm before the lm_head - once as separate kernels and once fused
+    into the down projection's activation load and the lm_head's prologue."""
     shapes = synth.decode_step_shapes()
     weights = []
     for i, (_, _, K, N) in enumerate(shapes):
@@ -328,6 +377,9 @@ def bench_decode_step(torch, mcv, synth, hbm, lm_w, ws_lm):
     outs = [torch.empty((1, N), dtype=torch.float16, device="cuda") for _, _, _, N in shapes]
     idx = torch.empty(1, dtype=torch.int64, device="cuda")
     x_lm = xs[1024]
+    gamma = (torch.randn(K_HIDDEN, device="cuda") * 0.1).to(torch.float16)
+    normed = torch.empty_like(x_lm)
+    act = torch.empty((1, 3584), dtype=torch.float16, device="cuda")
     same_input = {"linear_qkv", "linear_z", "linear_a", "linear_b", "full_q", "full_k", "full_v", "mlp_gate", "mlp_up"}
     groups, cur = [], []
     for i, (layer, name, K, N) in enumerate(shapes):
@@ -343,6 +395,11 @@ def bench_decode_step(torch, mcv, synth, hbm, lm_w, ws_lm):
     if cur:
         groups.append([j for _, j in cur])
     probs = [mcv.w4a16_problems([(xs[shapes[i][2]], weights[i], outs[i]) for i in grp]) for grp in groups]
+    # per layer: the gate / up outputs feeding its down projection
+    gate_up = {}
+    for i, (layer, name, _, _) in enumerate(shapes):
+        if name in ("mlp_gate", "mlp_up"):
+            gate_up.setdefault(layer, {})[name] = outs[i]
 
     def separate():
         for (_, _, K, N), w, o in zip(shapes, weights, outs):
@@ -353,10 +410,34 @@ def bench_decode_step(torch, mcv, synth, hbm, lm_w, ws_lm):
         for p in probs:
             mcv.matmul_w4a16_grouped(None, problems=p)
         mcv.lm_head_argmax(x_lm, lm_w, ws_lm, out_index=idx)
+
+    def grouped_neighbours(fused):
+        for grp, p in zip(groups, probs):
+            layer, name, _, _ = shapes[grp[0]]
+            if name == "mlp_down":
+                gu = gate_up[layer]
+                if fused:
+                    mcv.matmul_w4a16_silu_mul(gu["mlp_gate"], gu["mlp_up"], weights[grp[0]], outs[grp[0]])
+                else:
+                    mcv.silu_mul(gu["mlp_gate"], gu["mlp_up"], act)
+                    mcv.matmul_w4a16(act, weights[grp[0]], outs[grp[0]])
+                continue
+            mcv.matmul_w4a16_grouped(None, problems=p)
+        if fused:
+            mcv.lm_head_argmax_rmsnorm(x_lm, gamma, lm_w, ws_lm, out_index=idx)
+        else:
+            mcv.rms_norm(x_lm, gamma, normed)
+            mcv.lm_head_argmax(normed, lm_w, ws_lm, out_index=idx)
+
     byts = sum(synth.w4a16_bytes(1, K, N) for _, _, K, N in shapes) + VOCAB * K_HIDDEN * 2 + K_HIDDEN * 2
     res = {"config": "config3: 186 W4A16 GEMVs (24-layer hybrid LM) + fp16 lm_head argmax, M=1",
-           "bytes_per_token": byts, "roofline_us": round(byts / (hbm * 1e3), 2)}
-    for name, fn, launches in (("separate", separate, len(shapes) + 1), ("grouped", grouped, len(groups) + 1)):
+           "bytes_per_token": byts, "roofline_us": round(byts / (hbm * 1e3), 2),
+           "bytes_note": "weights and activations of the matmuls; the neighbours add < 0.1 % (a few KB per layer)"}
+    n_groups = len(groups)
+    variants = (("separate", separate, len(shapes) + 1), ("grouped", grouped, n_groups + 1),
+                ("grouped+neighbours_separate", lambda: grouped_neighbours(False), n_groups + 24 + 2),
+                ("grouped+neighbours_fused", lambda: grouped_neighbours(True), n_groups + 1))
+    for name, fn, launches in variants:
         fn()
         torch.cuda.synchronize()
         g = graph_of(torch, fn, torch.cuda.Stream())
@@ -639,6 +720,7 @@ def main():
             extras["w8a8"] = bench_w8a8(torch, mcv, synth, l2, hbm)
             extras["decode_step"] = bench_decode_step(torch, mcv, synth, hbm, w_copies[0], ws)
             extras["w4a16_gemm"] = bench_w4a16_gemm(torch, mcv, synth, l2, hbm, _tf)
+            extras["gemm_f16"] = bench_gemm_f16(torch, mcv, l2, hbm, _tf)
             extras["lm_head_w8a8"] = bench_lm_head_w8a8(torch, mcv, hbm, w_copies[0])
 
     if rank == 0:

@@ -169,9 +169,10 @@ int mcv_w4a16_pack_from_tiles_host(const int8_t* packed, int64_t tile_len,
                                    uint32_t* qweight_out, uint16_t* scales_out,
                                    uint32_t* zeros_out, int* zero_bias_out);
 
-/* out[m][n] = sum_k x[m][k] * w[k][n], M = 1..8, fp32 accumulation, fp16 out.
+/* out[m][n] = sum_k x[m][k] * w[k][n], M = 1..32, fp32 accumulation, fp16 out.
  * x fp16 [M][K], out fp16 [M][N]; group must be 128; x, qweight and scales
- * 16-byte aligned.
+ * 16-byte aligned.  M = 9..32 (batched decode) shares each dequantised weight
+ * fragment across up to four MMAs and needs K <= 8192.
  * Replaces matmul_w4a16 (src/csrc/lib/ops.cpp:1030-1095, ops.h:95-108; M=1
  * there) and its kernel op_kernel/matmul_w4a16_custom.cpp. */
 int mcv_w4a16_gemv(const void* x, const void* qweight, const void* scales, const void* zeros,
@@ -533,9 +534,10 @@ typedef struct mcv_decode_weights {
  * matmul_decode_dispatch (src/csrc/lib/decoder_layer.cpp:226-244): W8A8
  * (fused quantize + int8 GEMV + dequant) when the policy is enabled, the
  * W8A8 weight is present and M == 1; else W4A16 when present and M == 1;
- * else the dense weight (M <= 8).  Beyond the reference: with no dense
- * weight, M > 1 stays on the int4 weights (GEMV up to M = 8, the tcgen05
- * GEMM above) instead of failing.  MCV_ERR_NULL when no format fits. */
+ * else the dense weight (GEMV up to M = 8, the tcgen05 GEMM above, which
+ * needs dense_layout 0).  Beyond the reference: with no dense weight, M > 1
+ * stays on the int4 weights (GEMV up to M = 32, the tcgen05 GEMM above)
+ * instead of failing.  MCV_ERR_NULL when no format fits. */
 int mcv_matmul_decode_dispatch(const void* x, const mcv_decode_weights* w, void* out, int64_t M,
                                int64_t K, int64_t N, mcv_stream_t stream);
 

@@ -542,7 +542,146 @@ w4a16_ksplit_kernel(const __grid_constant__ GroupParams gp) {
     }
 }
 
+// Batched decode, M = 9..32 rows of x: the K-split schedule with each
+// dequantised A fragment feeding MT = ceil(M / 8) MMAs, one per 8 rows of x
+// (the MMA's N), so the dequant work per weight is paid once for up to 32
+// rows.  Lane (g, t) supplies x row 8T + g of tile T and ends with the
+// outputs of rows 8T + 2t, 8T + 2t + 1 for columns g, g + 8 of the strip.
+template <int MT, int KG>
+__global__ void __launch_bounds__(kWarps * 32)
+w4a16_ksplit_wide_kernel(const __grid_constant__ GroupParams gp, int M) {
+    __shared__ float4 red[kWarps][MT][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int strip = static_cast<int>(blockIdx.x);
+    const int pi = find_problem(gp, strip, 0);
+    const Problem& P = gp.p[pi];
+    const int K = P.K, G = K / kGroup, Gp = (G + 7) & ~7, zw = (G + 7) >> 3;
+    const int sl = strip - P.strip_begin;
+    const int col = sl * 16 + g;
+    uint4 v[KG][2];
+    float slo[KG], shi[KG];
+    int zlo[KG], zhi[KG];
+#pragma unroll
+    for (int j = 0; j < KG; ++j) {
+        const int gi = warp + j * kWarps;
+        v[j][0] = v[j][1] = make_uint4(0, 0, 0, 0);
+        slo[j] = shi[j] = 0.0f;
+        zlo[j] = zhi[j] = 0;
+        if (gi < G) {
+            const size_t base = (static_cast<size_t>(sl) * (K / 64) + 2 * gi) * 32 + lane;
+            v[j][0] = ld_stream(P.qw + base);
+            v[j][1] = ld_stream(P.qw + base + 32);
+            slo[j] = __half2float(P.s[static_cast<size_t>(col) * Gp + gi]);
+            shi[j] = __half2float(P.s[static_cast<size_t>(col + 8) * Gp + gi]);
+            zlo[j] = static_cast<int>((P.z[static_cast<size_t>(col) * zw + (gi >> 3)] >> (4 * (gi & 7))) & 0xfu);
+            zhi[j] = static_cast<int>((P.z[static_cast<size_t>(col + 8) * zw + (gi >> 3)] >> (4 * (gi & 7))) & 0xfu);
+        }
+    }
+    pdl_trigger();
+    pdl_wait();  // x may be the previous kernel's output
+    float acc[MT][4];
+#pragma unroll
+    for (int T = 0; T < MT; ++T) acc[T][0] = acc[T][1] = acc[T][2] = acc[T][3] = 0.0f;
+    constexpr uint32_t kMagic = 0x64006400u;
+    const __half2 inv16 = u32_as_h2(0x2c002c00u);
+#pragma unroll
+    for (int j = 0; j < KG; ++j) {
+        const int gi = warp + j * kWarps;
+        if (gi >= G) break;
+        const __half2 zl = u32_as_h2(h2_bits_1024_plus(zlo[j] + P.zero_bias));
+        const __half2 zh = u32_as_h2(h2_bits_neg_64_plus(zhi[j] + P.zero_bias));
+        float c[MT][4];
+#pragma unroll
+        for (int T = 0; T < MT; ++T) c[T][0] = c[T][1] = c[T][2] = c[T][3] = 0.0f;
+#pragma unroll
+        for (int qd = 0; qd < 2; ++qd) {
+            uint4 xv[MT][2];
+#pragma unroll
+            for (int T = 0; T < MT; ++T) {
+                xv[T][0] = xv[T][1] = make_uint4(0, 0, 0, 0);
+                const int row = 8 * T + g;
+                if (row < M) {
+                    const __half* xg = P.x + static_cast<size_t>(row) * K + gi * kGroup + qd * 64 + 16 * t;
+                    xv[T][0] = *reinterpret_cast<const uint4*>(xg);
+                    xv[T][1] = *reinterpret_cast<const uint4*>(xg + 8);
+                }
+            }
+            const uint4 vv = v[j][qd];
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const uint32_t w = jj == 0 ? vv.x : jj == 1 ? vv.y : jj == 2 ? vv.z : vv.w;
+                const uint32_t w8 = w >> 8;
+                uint32_t a[4];
+                a[0] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w, 0x000f000fu, kMagic)), zl));
+                a[1] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w, 0x00f000f0u, kMagic)), inv16, zh));
+                a[2] = h2_as_u32(__hsub2(u32_as_h2(lop3_and_or(w8, 0x000f000fu, kMagic)), zl));
+                a[3] = h2_as_u32(__hfma2(u32_as_h2(lop3_and_or(w8, 0x00f000f0u, kMagic)), inv16, zh));
+#pragma unroll
+                for (int T = 0; T < MT; ++T) {
+                    const uint4 xx = xv[T][jj >> 1];
+                    mma_16816(c[T], a, (jj & 1) ? xx.z : xx.x, (jj & 1) ? xx.w : xx.y);
+                }
+            }
+        }
+#pragma unroll
+        for (int T = 0; T < MT; ++T) {
+            acc[T][0] = fmaf(c[T][0], slo[j], acc[T][0]);
+            acc[T][1] = fmaf(c[T][1], slo[j], acc[T][1]);
+            acc[T][2] = fmaf(c[T][2], shi[j], acc[T][2]);
+            acc[T][3] = fmaf(c[T][3], shi[j], acc[T][3]);
+        }
+    }
+#pragma unroll
+    for (int T = 0; T < MT; ++T) red[warp][T][lane] = make_float4(acc[T][0], acc[T][1], acc[T][2], acc[T][3]);
+    __syncthreads();
+    // warps 0..MT-1 each finish one tile of 8 rows
+    if (warp < MT) {
+        const int T = warp;
+        float4 sum = red[0][T][lane];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) {
+            const float4 r = red[w][T][lane];
+            sum.x += r.x;
+            sum.y += r.y;
+            sum.z += r.z;
+            sum.w += r.w;
+        }
+        const int n0 = sl * 16;
+        const size_t N = static_cast<size_t>(P.N);
+        const int m0 = 8 * T + 2 * t;
+        if (m0 < M) {
+            if (n0 + g < P.N) P.out[m0 * N + n0 + g] = __float2half_rn(sum.x);
+            if (n0 + g + 8 < P.N) P.out[m0 * N + n0 + g + 8] = __float2half_rn(sum.z);
+        }
+        if (m0 + 1 < M) {
+            if (n0 + g < P.N) P.out[(m0 + 1) * N + n0 + g] = __float2half_rn(sum.y);
+            if (n0 + g + 8 < P.N) P.out[(m0 + 1) * N + n0 + g + 8] = __float2half_rn(sum.w);
+        }
+    }
+}
+
 int assign_strips(GroupParams& gp);
+
+template <int MT>
+int launch_wide_mt(GroupParams& gp, int M, cudaStream_t st) {
+    const int strips = assign_strips(gp);
+    int maxG = 0;
+    for (int i = 0; i < gp.count; ++i) maxG = std::max(maxG, gp.p[i].K / kGroup);
+    const int per_warp = (maxG + kWarps - 1) / kWarps;
+    auto go = [&](auto kern) { return launch(kern, dim3(strips), dim3(kWarps * 32), 0, st, gp, M); };
+    if (per_warp <= 1) return go(w4a16_ksplit_wide_kernel<MT, 1>);
+    if (per_warp <= 2) return go(w4a16_ksplit_wide_kernel<MT, 2>);
+    if (per_warp <= 4) return go(w4a16_ksplit_wide_kernel<MT, 4>);
+    if (per_warp <= 8) return go(w4a16_ksplit_wide_kernel<MT, 8>);
+    return fail(MCV_ERR_SHAPE, "w4a16_gemv: M > 8 needs K <= 8192");
+}
+
+int run_group_wide(GroupParams& gp, int M, cudaStream_t st) {
+    if (M <= 16) return launch_wide_mt<2>(gp, M, st);
+    if (M <= 24) return launch_wide_mt<3>(gp, M, st);
+    return launch_wide_mt<4>(gp, M, st);
+}
 
 // The K-split kernel for the down projection with silu_mul fused into its
 // activation load: x = silu(gate) * up (decoder_layer.cpp:1203-1204, the
@@ -708,6 +847,7 @@ int run_group_math(GroupParams& gp, int64_t M, cudaStream_t st) {
 }
 
 int run_group(GroupParams& gp, int64_t M, cudaStream_t st) {
+    if (M > 8) return run_group_wide(gp, static_cast<int>(M), st);
     switch (tuning(MCV_TUNE_W4A16_MATH)) {
         case 1: return run_group_math<0>(gp, M, st);
         case 2: return run_group_math<1>(gp, M, st);
@@ -961,7 +1101,7 @@ int mcv_w4a16_gemv_silu_mul(const void* gate, const void* up, const void* qweigh
 
 int mcv_w4a16_gemv_grouped(const mcv_w4a16_problem* problems, int count, int64_t M, mcv_stream_t stream) {
     if (!problems || count < 1) return fail(MCV_ERR_NULL, "w4a16_gemv: no problems");
-    if (M < 1 || M > 8) return fail(MCV_ERR_SHAPE, "w4a16_gemv: M must be 1..8");
+    if (M < 1 || M > 32) return fail(MCV_ERR_SHAPE, "w4a16_gemv: M must be 1..32");
     for (int i = 0; i < count; ++i) {
         const mcv_w4a16_problem& p = problems[i];
         if (!p.x || !p.qweight || !p.scales || !p.zeros || !p.out) return fail(MCV_ERR_NULL, "w4a16_gemv: null pointer");

@@ -204,3 +204,14 @@ def test_no_device_errors_recorded(cuda):
     """No bounded wait in any W4A16 kernel gave up during the tests above."""
     import mcv_b200
     assert mcv_b200.device_errors() == 0
+
+
+@pytest.mark.parametrize("M,K,N", [(9, 1024, 3584), (16, 1024, 4096), (24, 3584, 1024), (32, 1024, 3584),
+                                   (13, 8192, 64), (32, 128, 40)])
+def test_batched_decode_gemv(cuda, M, K, N):
+    """M = 9..32 on the widened GEMV (one dequantised fragment, up to four MMAs)."""
+    import mcv_b200
+    x, q, z, s = synth.w4a16_inputs(M, K, N, seed=M * 100 + K)
+    ref = oracle.w4a16_gemv(x, oracle.w4a16_fold_zeros(q, z), s, nthreads=8)
+    out = run_gemv(cuda, x, mcv_b200.pack_w4a16(q, z, s))
+    assert_f16_close(out, ref, what=f"batched M={M} K={K} N={N}")
