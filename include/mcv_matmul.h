@@ -64,10 +64,12 @@ void mcv_set_pdl(int enabled);
  *   its warps (K <= 8192), 3 = streaming kernel fed by warp-private
  *   bulk-copy rings; default: K-split below 4 strips per SM, else 3.
  *   MCV_TUNE_ROWS_BLOCKS_PER_SM: blocks per SM of the persistent lm_head /
- *   [N][K] GEMV grid (1..4; default 2).
+ *   [N][K] GEMV grid (1..4; default 4).
  *   MCV_TUNE_ROWS_PREFETCH: how many row steps ahead of its loads each warp
- *   of that grid warms L2 (1..16; -1 = no warm-up; default: 2 when each
- *   warp has at most 8 row steps, else none).
+ *   of that grid warms L2 (1..16; -1 = no warm-up; default: 1 when each
+ *   warp has at most 16 row steps, else none).
+ *   MCV_TUNE_ROWS_WALK: 1 = that grid's warps take rows strided by the grid,
+ *   2 = each warp a contiguous range (default).
  *   MCV_TUNE_GEMM_SPLIT_K: k slices (1..8, thread-block cluster along z) of
  *   mcv_w4a16_gemm; default: doubled while the output tiles times the
  *   slices fit the SMs and every slice keeps >= 4 stages of 64 k.
@@ -89,6 +91,7 @@ enum mcv_tuning_key {
     MCV_TUNE_W8A8_KERNEL = 6,
     MCV_TUNE_W4A16_GRID = 7,
     MCV_TUNE_W4A16_MATH = 8,
+    MCV_TUNE_ROWS_WALK = 9,
     MCV_TUNE_COUNT = 10
 };
 int mcv_set_tuning(int key, int value);
@@ -367,8 +370,11 @@ int mcv_lm_head_argmax_p2p(void* ctx, const void* x, const void* w, void* out_ke
  * the kernel's launch parameters when M * K <= 2048 (read during this call);
  * larger x is copied to x_dev first (pin x_host for an asynchronous copy).
  * When index_host is page-locked the kernel stores the indices into it
- * directly; otherwise they go through index_dev (M int64 on the device) and a
- * copy.  x_dev and index_dev are required either way.  Synchronous; same
+ * directly and the call returns as soon as they are there (the host watches
+ * that memory; the kernel may still be retiring, and later work on `stream`
+ * stays ordered after it); otherwise they go through index_dev (M int64 on
+ * the device), a copy and a stream synchronisation.  x_dev and index_dev are
+ * required either way.  The indices are final when the call returns; same
  * workspace rules as mcv_lm_head_argmax. */
 int mcv_lm_head_greedy_host(void* p2p_ctx, const void* x_host, void* x_dev, const void* norm_gamma, float norm_eps,
                             const void* w, void* index_dev, int64_t* index_host, int64_t M, int64_t K,

@@ -63,7 +63,21 @@ struct RowArgs {
     P2PArgs p2p;
     const __half* w_scale;  // int8 lm_head: per-row weight scales [N] (w then holds int8 rows)
     NormArgs norm;          // argmax: rms_norm of x in the prologue (norm.gamma null: x as given)
+    int contiguous;         // 1: each warp walks its own contiguous row range; 0: rows strided by the grid
 };
+
+// A warp's rows: [begin, end) in steps of `step`.  Contiguous ranges give
+// every warp the same row count to within one, so the last step of the
+// launch is not left partly filled (the strided walk's last step covers only
+// part of the warps: e.g. 31,012 rows on 4,736 warps is 3.27 steps of 2 rows).
+struct RowWalk {
+    int64_t begin, end, step;
+};
+__device__ __forceinline__ RowWalk row_walk(const RowArgs& a, int64_t gwarp, int64_t nwarps) {
+    if (a.contiguous)
+        return RowWalk{(gwarp * a.N) / nwarps, ((gwarp + 1) * a.N) / nwarps, kRowsPerStep};
+    return RowWalk{gwarp * kRowsPerStep, a.N, nwarps * kRowsPerStep};
+}
 
 __device__ __forceinline__ void st_relaxed_sys(uint64_t* p, uint64_t v) {
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -208,14 +222,15 @@ __device__ __forceinline__ void rows_body(const RowArgs& a, const uint4* xsrc) {
 
     // Prefetch this warp's first rows before waiting on the previous kernel.
     uint4 wv[kRowsPerStep][KCH];
-    int64_t r = gwarp * kRowsPerStep;
-    const int64_t step = nwarps * kRowsPerStep;
+    const RowWalk walk = row_walk(a, gwarp, nwarps);
+    int64_t r = walk.begin;
+    const int64_t step = walk.step, rend = walk.end;
 #pragma unroll
     for (int t = 0; t < kRowsPerStep; ++t)
 #pragma unroll
         for (int i = 0; i < KCH; ++i) {
             const int c = lane + 32 * i;
-            if (r + t < a.N && c < chunks) wv[t][i] = ld_stream(w4 + (r + t) * chunks + c);
+            if (r + t < rend && c < chunks) wv[t][i] = ld_stream(w4 + (r + t) * chunks + c);
         }
     // Warm L2 with this warp's next few row pairs too (bulk prefetch, no
     // registers): the weights never depend on the previous kernel, so their
@@ -223,7 +238,7 @@ __device__ __forceinline__ void rows_body(const RowArgs& a, const uint4* xsrc) {
     // Later steps keep the warm-up a.prefetch steps ahead of the loads.
     if (lane < kRowsPerStep * a.prefetch) {
         const int64_t pr = r + step * (1 + lane / kRowsPerStep) + (lane % kRowsPerStep);
-        if (pr < a.N) prefetch_l2(w4 + pr * chunks, static_cast<uint32_t>(a.K) * 2u);
+        if (pr < rend) prefetch_l2(w4 + pr * chunks, static_cast<uint32_t>(a.K) * 2u);
     }
     pdl_trigger();
     pdl_wait();
@@ -242,7 +257,7 @@ __device__ __forceinline__ void rows_body(const RowArgs& a, const uint4* xsrc) {
 #pragma unroll
     for (int m = 0; m < M; ++m) best[m] = 0;
 
-    while (r < a.N) {
+    while (r < rend) {
         float acc0[kRowsPerStep][M], acc1[kRowsPerStep][M];
 #pragma unroll
         for (int t = 0; t < kRowsPerStep; ++t)
@@ -269,14 +284,14 @@ __device__ __forceinline__ void rows_body(const RowArgs& a, const uint4* xsrc) {
         const int64_t rn = r + step;
         if (lane < kRowsPerStep && a.prefetch > 0) {
             const int64_t pr = rn + step * a.prefetch + lane;
-            if (pr < a.N) prefetch_l2(w4 + pr * chunks, static_cast<uint32_t>(a.K) * 2u);
+            if (pr < rend) prefetch_l2(w4 + pr * chunks, static_cast<uint32_t>(a.K) * 2u);
         }
 #pragma unroll
         for (int t = 0; t < kRowsPerStep; ++t)
 #pragma unroll
             for (int i = 0; i < KCH; ++i) {
                 const int c = lane + 32 * i;
-                if (rn + t < a.N && c < chunks) wv[t][i] = ld_stream(w4 + (rn + t) * chunks + c);
+                if (rn + t < rend && c < chunks) wv[t][i] = ld_stream(w4 + (rn + t) * chunks + c);
             }
 #pragma unroll
         for (int t = 0; t < kRowsPerStep; ++t) {
@@ -284,7 +299,7 @@ __device__ __forceinline__ void rows_body(const RowArgs& a, const uint4* xsrc) {
 #pragma unroll
             for (int m = 0; m < M; ++m) {
                 float v = warp_sum(acc0[t][m] + acc1[t][m]);
-                if (row < a.N) {
+                if (row < rend) {
                     if constexpr (ARGMAX) {
                         if constexpr (FP16_LOGITS) v = __half2float(__float2half_rn(v));
                         const uint64_t key = argmax_key(v, static_cast<uint32_t>(a.n_offset + row));
@@ -402,23 +417,29 @@ int row_grid(int64_t N) {
     const int64_t warps_needed = (N + kRowsPerStep - 1) / kRowsPerStep;
     const int64_t blocks_needed = (warps_needed + kRowWarps - 1) / kRowWarps;
     const int t = tuning(MCV_TUNE_ROWS_BLOCKS_PER_SM);
-    const int bps = (t >= 1 && t <= 4) ? t : 2;  // <= 4: the workspace is sized for 4 blocks per SM
+    const int bps = (t >= 1 && t <= 4) ? t : 4;  // <= 4: the workspace is sized for 4 blocks per SM
     const int64_t cap = static_cast<int64_t>(sm_count()) * bps;
     return static_cast<int>(blocks_needed < cap ? blocks_needed : cap);
 }
 
 // L2 warm-up distance in row steps: MCV_TUNE_ROWS_PREFETCH 1..16, -1 none.
-// Default (measured on B200, K=1024): two steps ahead when each warp has at
-// most 8 row steps (a vocabulary shard of ~31k rows: 13.1 vs 14.0 us), none
-// on longer runs, where the warm-up only competes with the demand loads
-// (248k rows: 76.5 vs 83.7 us with a 3-step warm-up).
+// Default: one step ahead when each warp walks at most 16 steps (a
+// vocabulary shard of up to ~150k rows on 4 blocks of 8 warps per SM), none
+// on longer walks, where the warm-up only competes with the demand loads.
+// Measured on B200, K = 1024, 4 blocks per SM, strided walk: 31,012 rows
+// 12.6 us with one step against 14.3 us with none and 13.8 us with two.
 int row_prefetch(int64_t N, int grid) {
     const int t = tuning(MCV_TUNE_ROWS_PREFETCH);
     if (t < 0) return 0;
     if (t >= 1 && t <= 16) return t;
-    const int64_t per_step = static_cast<int64_t>(grid) * kRowWarps * kRowsPerStep;
-    return (N + per_step - 1) / per_step <= 8 ? 2 : 0;
+    const int64_t warps = static_cast<int64_t>(grid) * kRowWarps;
+    const int64_t steps = ((N + warps - 1) / warps + kRowsPerStep - 1) / kRowsPerStep;
+    return steps <= 16 ? 1 : 0;
 }
+
+// Row walk: MCV_TUNE_ROWS_WALK 1 = strided by the grid, 2 = contiguous
+// ranges per warp (default).
+int row_contiguous() { return tuning(MCV_TUNE_ROWS_WALK) == 1 ? 0 : 1; }
 
 template <int M, bool ARGMAX, bool FP16, class Args>
 int launch_rows_m(int kch, const Args& args, cudaStream_t s, int grid) {
@@ -495,21 +516,22 @@ rows_w8_kernel(RowArgs a) {
 
     uint4 wv[kRowsPerStep][KCH];
     float wsc[kRowsPerStep];
-    int64_t r = gwarp * kRowsPerStep;
-    const int64_t step = nwarps * kRowsPerStep;
+    const RowWalk walk = row_walk(a, gwarp, nwarps);
+    int64_t r = walk.begin;
+    const int64_t step = walk.step, rend = walk.end;
 #pragma unroll
     for (int t = 0; t < kRowsPerStep; ++t) {
-        wsc[t] = r + t < a.N ? __half2float(a.w_scale[r + t]) : 0.0f;
+        wsc[t] = r + t < rend ? __half2float(a.w_scale[r + t]) : 0.0f;
 #pragma unroll
         for (int i = 0; i < KCH; ++i) {
             const int c = lane + 32 * i;
             wv[t][i] = make_uint4(0, 0, 0, 0);
-            if (r + t < a.N && c < chunks) wv[t][i] = ld_stream(w4 + (r + t) * chunks + c);
+            if (r + t < rend && c < chunks) wv[t][i] = ld_stream(w4 + (r + t) * chunks + c);
         }
     }
     if (lane < kRowsPerStep * a.prefetch) {
         const int64_t pr = r + step * (1 + lane / kRowsPerStep) + (lane % kRowsPerStep);
-        if (pr < a.N) prefetch_l2(w4 + pr * chunks, static_cast<uint32_t>(a.K));
+        if (pr < rend) prefetch_l2(w4 + pr * chunks, static_cast<uint32_t>(a.K));
     }
     pdl_trigger();
     pdl_wait();
@@ -521,7 +543,7 @@ rows_w8_kernel(RowArgs a) {
 #pragma unroll
     for (int m = 0; m < M; ++m) best[m] = 0;
 
-    while (r < a.N) {
+    while (r < rend) {
         int acc[kRowsPerStep][M];
 #pragma unroll
         for (int t = 0; t < kRowsPerStep; ++t)
@@ -550,16 +572,16 @@ rows_w8_kernel(RowArgs a) {
         const int64_t rn = r + step;
         if (lane < kRowsPerStep && a.prefetch > 0) {
             const int64_t pr = rn + step * a.prefetch + lane;
-            if (pr < a.N) prefetch_l2(w4 + pr * chunks, static_cast<uint32_t>(a.K));
+            if (pr < rend) prefetch_l2(w4 + pr * chunks, static_cast<uint32_t>(a.K));
         }
         float wsn[kRowsPerStep];
 #pragma unroll
         for (int t = 0; t < kRowsPerStep; ++t) {
-            wsn[t] = rn + t < a.N ? __half2float(a.w_scale[rn + t]) : 0.0f;
+            wsn[t] = rn + t < rend ? __half2float(a.w_scale[rn + t]) : 0.0f;
 #pragma unroll
             for (int i = 0; i < KCH; ++i) {
                 const int c = lane + 32 * i;
-                if (rn + t < a.N && c < chunks) wv[t][i] = ld_stream(w4 + (rn + t) * chunks + c);
+                if (rn + t < rend && c < chunks) wv[t][i] = ld_stream(w4 + (rn + t) * chunks + c);
             }
         }
 #pragma unroll
@@ -570,7 +592,7 @@ rows_w8_kernel(RowArgs a) {
                 int v = acc[t][m];
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (row < a.N) {
+                if (row < rend) {
                     const __half h = __float2half_rn(__fmul_rn(__fmul_rn(__int2float_rn(v), wsc[t]), xscale_s[m]));
                     const uint64_t key = argmax_key(h2f_flush_subnormal(h), static_cast<uint32_t>(a.n_offset + row));
                     best[m] = key > best[m] ? key : best[m];
@@ -648,6 +670,7 @@ int lm_head_argmax_impl_p2p(const void* x, const void* w, void* out_key, void* o
     const int grid = row_grid(N);
     RowArgs a{};
     a.prefetch = row_prefetch(N, grid);
+    a.contiguous = row_contiguous();
     a.x = static_cast<const __half*>(x);
     a.w = static_cast<const __half*>(w);
     a.counter = static_cast<unsigned*>(ws);
@@ -694,6 +717,7 @@ int lm_head_argmax_w8a8_impl(const void* x, const void* w, const void* w_scale, 
     const int grid = static_cast<int>(blocks_needed < cap ? blocks_needed : cap);
     RowArgs a{};
     a.prefetch = row_prefetch(N, grid);
+    a.contiguous = row_contiguous();
     a.x = static_cast<const __half*>(x);
     a.w = static_cast<const __half*>(w);
     a.w_scale = static_cast<const __half*>(w_scale);
@@ -746,6 +770,7 @@ int mcv_gemv_f16(const void* x, const void* w, void* out, int64_t M, int64_t K, 
         if (N > 0x7fffffffLL) return fail(MCV_ERR_SHAPE, "gemv_f16: N too large");
         RowArgs a{};
         a.prefetch = row_prefetch(N, row_grid(N));
+        a.contiguous = row_contiguous();
         a.x = static_cast<const __half*>(x);
         a.w = static_cast<const __half*>(w);
         a.out = static_cast<__half*>(out);

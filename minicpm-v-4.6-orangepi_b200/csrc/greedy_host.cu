@@ -5,6 +5,9 @@
 // the fused GEMV + argmax stores the index straight into page-locked host
 // memory (else one 8-byte copy-out), then the stream is synchronised: one
 // library call and, for a 1024-wide row, one queued GPU operation per token.
+#include <chrono>
+#include <cstdint>
+
 #include "common.cuh"
 
 namespace mcv {
@@ -55,6 +58,16 @@ int mcv_lm_head_greedy_host(void* p2p_ctx, const void* x_host, void* x_dev, cons
         out = pa_out.devicePointer;
     else
         (void)cudaGetLastError();  // pageable memory: not an error, copy out below
+    // With the index stored straight into page-locked memory, the host
+    // watches that memory instead of waiting for the stream: the answer is
+    // there as soon as the kernel's last block has stored it, ahead of the
+    // grid's retirement and the stream's completion signal.
+    constexpr int64_t kSentinel = INT64_MIN;
+    volatile int64_t* watch = nullptr;
+    if (out != index_dev) {
+        watch = index_host;
+        for (int64_t m = 0; m < M; ++m) watch[m] = kSentinel;
+    }
     const int st = lm_head_argmax_impl_p2p(by_param ? nullptr : x_dev, w, nullptr, out, M, K, N_shard, n_offset,
                                            fp16_logits, workspace, workspace_bytes, s, pa,
                                            by_param ? x_host : nullptr, norm_gamma ? &norm : nullptr);
@@ -64,6 +77,17 @@ int mcv_lm_head_greedy_host(void* p2p_ctx, const void* x_host, void* x_dev, cons
         e = cudaMemcpyAsync(index_host, index_dev, static_cast<size_t>(M) * sizeof(int64_t), cudaMemcpyDeviceToHost,
                             s);
         if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(index out)");
+    }
+    if (watch) {
+        // bounded: after 10 s fall through to the stream wait, which reports
+        // whatever stopped the kernel
+        const auto t0 = std::chrono::steady_clock::now();
+        for (uint32_t i = 1;; ++i) {
+            bool all = true;
+            for (int64_t m = 0; m < M; ++m) all = all && watch[m] != kSentinel;
+            if (all) return MCV_OK;
+            if ((i & 1023u) == 0 && std::chrono::steady_clock::now() - t0 > std::chrono::seconds(10)) break;
+        }
     }
     e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");

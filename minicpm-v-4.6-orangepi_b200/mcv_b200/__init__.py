@@ -171,6 +171,7 @@ TUNE_GEMM_SPLIT_K = 5
 TUNE_W8A8_KERNEL = 6
 TUNE_W4A16_GRID = 7
 TUNE_W4A16_MATH = 8
+TUNE_ROWS_WALK = 9
 
 
 def device_errors() -> int:
