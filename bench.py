@@ -367,7 +367,7 @@ def bench_decode_step(torch, mcv, synth, hbm, lm_w, ws_lm):
     '+neighbours' variants add what sits between the matmuls on the hot
     path - silu_mul between each layer's gate/up and down projections and the
     final rms_norm before the lm_head - once as separate kernels and once fused
-    into the down projection's activation load and the lm_head's prologue."""
+    into the gate / up launch's epilogue (SwiGLU) and the lm_head's prologue."""
     shapes = synth.decode_step_shapes()
     weights = []
     for i, (_, _, K, N) in enumerate(shapes):
@@ -379,7 +379,6 @@ def bench_decode_step(torch, mcv, synth, hbm, lm_w, ws_lm):
     x_lm = xs[1024]
     gamma = (torch.randn(K_HIDDEN, device="cuda") * 0.1).to(torch.float16)
     normed = torch.empty_like(x_lm)
-    act = torch.empty((1, 3584), dtype=torch.float16, device="cuda")
     same_input = {"linear_qkv", "linear_z", "linear_a", "linear_b", "full_q", "full_k", "full_v", "mlp_gate", "mlp_up"}
     groups, cur = [], []
     for i, (layer, name, K, N) in enumerate(shapes):
@@ -395,11 +394,14 @@ def bench_decode_step(torch, mcv, synth, hbm, lm_w, ws_lm):
     if cur:
         groups.append([j for _, j in cur])
     probs = [mcv.w4a16_problems([(xs[shapes[i][2]], weights[i], outs[i]) for i in grp]) for grp in groups]
-    # per layer: the gate / up outputs feeding its down projection
-    gate_up = {}
+    # per layer: the gate / up outputs feeding its down projection, and the
+    # down projection's input (the SwiGLU activation)
+    gate_up, gate_up_w = {}, {}
     for i, (layer, name, _, _) in enumerate(shapes):
         if name in ("mlp_gate", "mlp_up"):
             gate_up.setdefault(layer, {})[name] = outs[i]
+            gate_up_w.setdefault(layer, {})[name] = weights[i]
+    acts = {layer: torch.empty((1, 3584), dtype=torch.float16, device="cuda") for layer in gate_up}
 
     def separate():
         for (_, _, K, N), w, o in zip(shapes, weights, outs):
@@ -414,13 +416,17 @@ def bench_decode_step(torch, mcv, synth, hbm, lm_w, ws_lm):
     def grouped_neighbours(fused):
         for grp, p in zip(groups, probs):
             layer, name, _, _ = shapes[grp[0]]
-            if name == "mlp_down":
-                gu = gate_up[layer]
+            if name == "mlp_gate":  # the gate / up group
                 if fused:
-                    mcv.matmul_w4a16_silu_mul(gu["mlp_gate"], gu["mlp_up"], weights[grp[0]], outs[grp[0]])
+                    w = gate_up_w[layer]
+                    mcv.matmul_w4a16_gate_up_silu(xs[1024], w["mlp_gate"], w["mlp_up"], acts[layer])
                 else:
-                    mcv.silu_mul(gu["mlp_gate"], gu["mlp_up"], act)
-                    mcv.matmul_w4a16(act, weights[grp[0]], outs[grp[0]])
+                    mcv.matmul_w4a16_grouped(None, problems=p)
+                    gu = gate_up[layer]
+                    mcv.silu_mul(gu["mlp_gate"], gu["mlp_up"], acts[layer])
+                continue
+            if name == "mlp_down":
+                mcv.matmul_w4a16(acts[layer], weights[grp[0]], outs[grp[0]])
                 continue
             mcv.matmul_w4a16_grouped(None, problems=p)
         if fused:

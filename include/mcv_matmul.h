@@ -64,12 +64,12 @@ void mcv_set_pdl(int enabled);
  *   its warps (K <= 8192), 3 = streaming kernel fed by warp-private
  *   bulk-copy rings; default: K-split below 4 strips per SM, else 3.
  *   MCV_TUNE_ROWS_BLOCKS_PER_SM: blocks per SM of the persistent lm_head /
- *   [N][K] GEMV grid (1..4; default 4).
+ *   [N][K] GEMV grid (1..4; default 4 up to 600 rows per SM, else 2).
  *   MCV_TUNE_ROWS_PREFETCH: how many row steps ahead of its loads each warp
- *   of that grid warms L2 (1..16; -1 = no warm-up; default: 1 when each
- *   warp has at most 16 row steps, else none).
- *   MCV_TUNE_ROWS_WALK: 1 = that grid's warps take rows strided by the grid,
- *   2 = each warp a contiguous range (default).
+ *   of that grid warms L2 (1..16; -1 = no warm-up; default: 1 up to 600
+ *   rows per SM, else none).
+ *   MCV_TUNE_ROWS_WALK: 1 = that grid's warps take rows strided by the grid
+ *   (default), 2 = each warp a contiguous range.
  *   MCV_TUNE_GEMM_SPLIT_K: k slices (1..8, thread-block cluster along z) of
  *   mcv_w4a16_gemm; default: doubled while the output tiles times the
  *   slices fit the SMs and every slice keeps >= 4 stages of 64 k.
@@ -215,17 +215,17 @@ typedef struct mcv_w4a16_problem {
 int mcv_w4a16_gemv_grouped(const mcv_w4a16_problem* problems, int count, int64_t M,
                            mcv_stream_t stream);
 
-/* The down projection with silu_mul fused into its activation load:
- * out fp16 [M][N] = (silu(gate) * up) [M][K] . W over an mcv-int4 weight, with
- * gate and up fp16 [M][K] (the gate/up projections' outputs).  The activation
- * is formed per element as the silu_mul kernel does (fp32
- * g / (1 + exp(-g)) * u, rounded to fp16; op_kernel/silu_mul_custom.cpp:63-72),
- * so the result equals mcv_silu_mul followed by mcv_w4a16_gemv.  Replaces
- * silu_mul + matmul_decode_dispatch(down) of decoder_layer.cpp:1203-1204.
- * M = 1..8, K <= 8192 (multiple of 128), group 128. */
-int mcv_w4a16_gemv_silu_mul(const void* gate, const void* up, const void* qweight, const void* scales,
-                            const void* zeros, int zero_bias, void* out, int64_t M, int64_t K, int64_t N,
-                            int64_t group, mcv_stream_t stream);
+/* The MLP's gate and up projections with SwiGLU in the epilogue:
+ * act fp16 [M][N] = silu_mul(x . Wg, x . Wu) for x fp16 [M][K] and two mcv-int4
+ * weights of equal K and N (the problems' x and out fields are ignored).  The
+ * gate and up sums are rounded to fp16 - the projections' output type - and
+ * combined exactly as mcv_silu_mul does (fp32 g / (1 + exp(-g)) * u,
+ * op_kernel/silu_mul_custom.cpp:63-72), in one launch and with no gate / up
+ * round trip through memory.  Replaces the gate and up matmul_decode_dispatch
+ * calls and the silu_mul of decoder_layer.cpp:1186-1203.  M = 1..8,
+ * K <= 4096 (multiple of 128), group 128. */
+int mcv_w4a16_gemv_gate_up_silu(const void* x, const mcv_w4a16_problem* gate, const mcv_w4a16_problem* up, void* act,
+                                int64_t M, mcv_stream_t stream);
 
 /* ======================================================================== */
 /* dense fp16 GEMV and the lm_head                                          */

@@ -84,6 +84,20 @@ void matmul_w4a16(const T& x, const W4A16Weight& w, T& out, cudaStream_t stream,
     finish(stream, sync, "matmul_w4a16");
 }
 
+/* The MLP's gate / up projections and their silu_mul in one launch:
+ * act [M,N] = silu_mul(x . gate, x . up) (decoder_layer.cpp:1186-1203). */
+template <class T>
+void matmul_w4a16_gate_up_silu(const T& x, const W4A16Weight& gate, const W4A16Weight& up, T& act,
+                               cudaStream_t stream, bool sync = false) {
+    detail::need_rank2(x, "matmul_w4a16_gate_up_silu");
+    const mcv_w4a16_problem g{nullptr, gate.qweight, gate.scales, gate.zeros, nullptr, static_cast<int32_t>(gate.K),
+                              static_cast<int32_t>(gate.N), 128, gate.zero_bias};
+    const mcv_w4a16_problem u{nullptr, up.qweight, up.scales, up.zeros, nullptr, static_cast<int32_t>(up.K),
+                              static_cast<int32_t>(up.N), 128, up.zero_bias};
+    check(mcv_w4a16_gemv_gate_up_silu(x.data(), &g, &u, act.data(), x.shape()[0], stream), "matmul_w4a16_gate_up_silu");
+    finish(stream, sync, "matmul_w4a16_gate_up_silu");
+}
+
 /* out [M,N] = a [M,K] . B with b stored [N,K] or [K,N], told apart by a's K
  * as the reference does (ops.cpp:165-171): the GEMV for M <= 8, the
  * tensor-core GEMM beyond ([N,K] weights only).  ops.h:19. */

@@ -66,10 +66,8 @@ struct RowArgs {
     int contiguous;         // 1: each warp walks its own contiguous row range; 0: rows strided by the grid
 };
 
-// A warp's rows: [begin, end) in steps of `step`.  Contiguous ranges give
-// every warp the same row count to within one, so the last step of the
-// launch is not left partly filled (the strided walk's last step covers only
-// part of the warps: e.g. 31,012 rows on 4,736 warps is 3.27 steps of 2 rows).
+// A warp's rows: [begin, end) in steps of `step`, either strided by the grid
+// (rows r, r + 2W, ...) or one contiguous range per warp.
 struct RowWalk {
     int64_t begin, end, step;
 };
@@ -411,35 +409,43 @@ __global__ void key_to_index_kernel(const uint64_t* __restrict__ key, int64_t* _
     if (m < M) out[m] = key[m] == 0 ? -1 : static_cast<int64_t>(0xffffffffu - static_cast<uint32_t>(key[m] & 0xffffffffu));
 }
 
+// Rows per SM below which the short-walk settings apply (4 blocks per SM,
+// one-step L2 warm-up): a vocabulary shard on 4 or 8 GPUs.
+constexpr int64_t kShortWalkRowsPerSm = 600;
+
 int row_grid(int64_t N) {
     // persistent grid: up to 4 blocks of 256 threads per SM, never more
-    // blocks than there are row pairs to hand out
+    // blocks than there are row pairs to hand out.  Default: 4 blocks per SM
+    // on short walks, 2 on long ones (measured on B200, K = 1024, strided
+    // walk: 31,012 rows 13.1 vs 13.8 us, 62,024 rows 22.8 vs 23.4 us, but
+    // 124,047 rows 45.3 vs 41.2 us and 248,094 rows 84.6 vs 76.7 us).
     const int64_t warps_needed = (N + kRowsPerStep - 1) / kRowsPerStep;
     const int64_t blocks_needed = (warps_needed + kRowWarps - 1) / kRowWarps;
     const int t = tuning(MCV_TUNE_ROWS_BLOCKS_PER_SM);
-    const int bps = (t >= 1 && t <= 4) ? t : 4;  // <= 4: the workspace is sized for 4 blocks per SM
+    const bool short_walk = N <= kShortWalkRowsPerSm * sm_count();
+    const int bps = (t >= 1 && t <= 4) ? t : (short_walk ? 4 : 2);  // <= 4: the workspace is sized for 4
     const int64_t cap = static_cast<int64_t>(sm_count()) * bps;
     return static_cast<int>(blocks_needed < cap ? blocks_needed : cap);
 }
 
 // L2 warm-up distance in row steps: MCV_TUNE_ROWS_PREFETCH 1..16, -1 none.
-// Default: one step ahead when each warp walks at most 16 steps (a
-// vocabulary shard of up to ~150k rows on 4 blocks of 8 warps per SM), none
-// on longer walks, where the warm-up only competes with the demand loads.
-// Measured on B200, K = 1024, 4 blocks per SM, strided walk: 31,012 rows
-// 12.6 us with one step against 14.3 us with none and 13.8 us with two.
+// Default: one step ahead on short walks (see row_grid), none on long ones,
+// where the warm-up only competes with the demand loads.  Measured on B200,
+// K = 1024, 4 blocks per SM: 31,012 rows 13.1 us with one step against 14.7
+// with none and 15.0 with two; 248,094 rows on 2 blocks per SM 76.7 us with
+// none against 82.9 with one.
 int row_prefetch(int64_t N, int grid) {
+    (void)grid;
     const int t = tuning(MCV_TUNE_ROWS_PREFETCH);
     if (t < 0) return 0;
     if (t >= 1 && t <= 16) return t;
-    const int64_t warps = static_cast<int64_t>(grid) * kRowWarps;
-    const int64_t steps = ((N + warps - 1) / warps + kRowsPerStep - 1) / kRowsPerStep;
-    return steps <= 16 ? 1 : 0;
+    return N <= kShortWalkRowsPerSm * sm_count() ? 1 : 0;
 }
 
-// Row walk: MCV_TUNE_ROWS_WALK 1 = strided by the grid, 2 = contiguous
-// ranges per warp (default).
-int row_contiguous() { return tuning(MCV_TUNE_ROWS_WALK) == 1 ? 0 : 1; }
+// Row walk: MCV_TUNE_ROWS_WALK 1 = rows strided by the grid (default), 2 =
+// a contiguous range per warp (every warp within one row of the same count,
+// but measured 3-6 % slower at every size from 31k to 248k rows).
+int row_contiguous() { return tuning(MCV_TUNE_ROWS_WALK) == 2 ? 1 : 0; }
 
 template <int M, bool ARGMAX, bool FP16, class Args>
 int launch_rows_m(int kch, const Args& args, cudaStream_t s, int grid) {

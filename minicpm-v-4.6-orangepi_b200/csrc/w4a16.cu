@@ -683,21 +683,23 @@ int run_group_wide(GroupParams& gp, int M, cudaStream_t st) {
     return launch_wide_mt<4>(gp, M, st);
 }
 
-// The K-split kernel for the down projection with silu_mul fused into its
-// activation load: x = silu(gate) * up (decoder_layer.cpp:1203-1204, the
-// silu_mul kernel's arithmetic in neighbours.cuh).  Each warp turns exactly
-// the activation slices of its own 128-k groups (M rows x 128) into a
-// warp-private shared-memory tile, all 32 lanes sharing the exp work, then
-// runs the same MMAs as w4a16_ksplit_kernel reading x from that tile.
+// The MLP's gate and up projections with SwiGLU in the epilogue
+// (decoder_layer.cpp:1186-1203): act = silu_mul(x . Wg, x . Wu).  Block b
+// computes strip b of both weights - warps 0-3 the gate, warps 4-7 the up
+// projection, each warp a quarter of the 128-k groups - so every lane ends
+// with the gate and up sums of the same (row, column) pairs.  Each is rounded
+// to fp16 (the projections' output type) and combined as the silu_mul kernel
+// does, so one launch replaces the grouped gate/up launch plus the silu_mul
+// launch, and the fp16 gate and up never travel through memory.
 template <int M, int KG>
 __global__ void __launch_bounds__(kWarps * 32)
-w4a16_ksplit_silu_kernel(const __grid_constant__ GroupParams gp, const __half* __restrict__ up) {
+w4a16_gate_up_silu_kernel(const __grid_constant__ GroupParams gp) {
     __shared__ float4 red[kWarps][32];
-    extern __shared__ __align__(16) __half xsilu[];  // [warp][KG][M][128]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int strip = static_cast<int>(blockIdx.x);
-    const Problem& P = gp.p[0];
+    const int wq = warp & 3;
+    const Problem& P = gp.p[warp >> 2];  // 0: gate, 1: up
     const int K = P.K, G = K / kGroup, Gp = (G + 7) & ~7, zw = (G + 7) >> 3;
     const int col = strip * 16 + g;
     uint4 v[KG][2];
@@ -705,7 +707,7 @@ w4a16_ksplit_silu_kernel(const __grid_constant__ GroupParams gp, const __half* _
     int zlo[KG], zhi[KG];
 #pragma unroll
     for (int j = 0; j < KG; ++j) {
-        const int gi = warp + j * kWarps;
+        const int gi = wq + j * 4;
         v[j][0] = v[j][1] = make_uint4(0, 0, 0, 0);
         slo[j] = shi[j] = 0.0f;
         zlo[j] = zhi[j] = 0;
@@ -720,29 +722,15 @@ w4a16_ksplit_silu_kernel(const __grid_constant__ GroupParams gp, const __half* _
         }
     }
     pdl_trigger();
-    pdl_wait();  // gate and up are the previous kernel's outputs
-    __half* xw = xsilu + static_cast<size_t>(warp) * KG * M * kGroup;
-#pragma unroll
-    for (int j = 0; j < KG; ++j) {
-        const int gi = warp + j * kWarps;
-        if (gi >= G) break;
-        for (int e = lane; e < M * (kGroup / 8); e += 32) {
-            const int m = e / (kGroup / 8), c = e % (kGroup / 8);
-            const size_t off = static_cast<size_t>(m) * K + gi * kGroup + c * 8;
-            const uint4 gv = *reinterpret_cast<const uint4*>(P.x + off);
-            const uint4 uv = *reinterpret_cast<const uint4*>(up + off);
-            *reinterpret_cast<uint4*>(xw + (j * M + m) * kGroup + c * 8) = silu_mul8(gv, uv);
-        }
-    }
-    __syncwarp();
+    pdl_wait();  // x may be the previous kernel's output
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int j = 0; j < KG; ++j) {
-        const int gi = warp + j * kWarps;
+        const int gi = wq + j * 4;
         if (gi >= G) break;
         float d[4];
-        group_mma<M>(v[j], xw + (j * M + (g < M ? g : 0)) * kGroup + 16 * t, g, zlo[j] + P.zero_bias,
-                     zhi[j] + P.zero_bias, d);
+        group_mma<M, 1>(v[j], P.x + static_cast<size_t>(g) * K + gi * kGroup + 16 * t, g, zlo[j] + P.zero_bias,
+                        zhi[j] + P.zero_bias, d);
         acc[0] = fmaf(d[0], slo[j], acc[0]);
         acc[1] = fmaf(d[1], slo[j], acc[1]);
         acc[2] = fmaf(d[2], shi[j], acc[2]);
@@ -751,37 +739,37 @@ w4a16_ksplit_silu_kernel(const __grid_constant__ GroupParams gp, const __half* _
     red[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
     __syncthreads();
     if (warp == 0) {
-        float4 sum = red[0][lane];
+        float4 gs = red[0][lane], us = red[4][lane];
 #pragma unroll
-        for (int w = 1; w < kWarps; ++w) {
-            const float4 r = red[w][lane];
-            sum.x += r.x;
-            sum.y += r.y;
-            sum.z += r.z;
-            sum.w += r.w;
+        for (int w = 1; w < 4; ++w) {
+            const float4 a = red[w][lane], b = red[4 + w][lane];
+            gs.x += a.x, gs.y += a.y, gs.z += a.z, gs.w += a.w;
+            us.x += b.x, us.y += b.y, us.z += b.z, us.w += b.w;
         }
-        const float out4[4] = {sum.x, sum.y, sum.z, sum.w};
-        store_strip<M>(P, strip, lane, out4);
+        const Problem& Q = gp.p[0];
+        const int n0 = strip * 16;
+        const size_t N = static_cast<size_t>(Q.N);
+        const int m0 = 2 * t;
+        auto put = [&](int m, int n, float gv, float uv) {
+            if (m < M && n < Q.N) Q.out[m * N + n] = silu_mul1(__float2half_rn(gv), __float2half_rn(uv));
+        };
+        put(m0, n0 + g, gs.x, us.x);
+        put(m0, n0 + g + 8, gs.z, us.z);
+        put(m0 + 1, n0 + g, gs.y, us.y);
+        put(m0 + 1, n0 + g + 8, gs.w, us.w);
     }
 }
 
 template <int M>
-int launch_silu_m(GroupParams& gp, const __half* up, cudaStream_t st) {
-    const int strips = assign_strips(gp);
+int launch_gate_up_m(GroupParams& gp, cudaStream_t st) {
+    const int strips = static_cast<int>(padded_n(gp.p[0].N) / 16);
     const int G = gp.p[0].K / kGroup;
-    const int per_warp = (G + kWarps - 1) / kWarps;
-    auto go = [&](auto kern, int kg) -> int {
-        const size_t smem = static_cast<size_t>(kWarps) * kg * M * kGroup * 2;
-        if (smem > 48 * 1024) {
-            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a16_ksplit_silu)");
-        }
-        return launch(kern, dim3(strips), dim3(kWarps * 32), smem, st, gp, up);
-    };
-    if (per_warp <= 1) return go(w4a16_ksplit_silu_kernel<M, 1>, 1);
-    if (per_warp <= 2) return go(w4a16_ksplit_silu_kernel<M, 2>, 2);
-    if (per_warp <= 4) return go(w4a16_ksplit_silu_kernel<M, 4>, 4);
-    return go(w4a16_ksplit_silu_kernel<M, 8>, 8);
+    const int per_warp = (G + 3) / 4;
+    auto go = [&](auto kern) { return launch(kern, dim3(strips), dim3(kWarps * 32), 0, st, gp); };
+    if (per_warp <= 1) return go(w4a16_gate_up_silu_kernel<M, 1>);
+    if (per_warp <= 2) return go(w4a16_gate_up_silu_kernel<M, 2>);
+    if (per_warp <= 4) return go(w4a16_gate_up_silu_kernel<M, 4>);
+    return go(w4a16_gate_up_silu_kernel<M, 8>);
 }
 
 int assign_strips(GroupParams& gp) {
@@ -1068,34 +1056,39 @@ int mcv_w4a16_gemv(const void* x, const void* qweight, const void* scales, const
     return mcv_w4a16_gemv_grouped(&p, 1, M, stream);
 }
 
-int mcv_w4a16_gemv_silu_mul(const void* gate, const void* up, const void* qweight, const void* scales,
-                            const void* zeros, int zero_bias, void* out, int64_t M, int64_t K, int64_t N,
-                            int64_t group, mcv_stream_t stream) {
-    if (!gate || !up || !qweight || !scales || !zeros || !out) return fail(MCV_ERR_NULL, "w4a16_gemv_silu_mul: null pointer");
-    if (M < 1 || M > 8) return fail(MCV_ERR_SHAPE, "w4a16_gemv_silu_mul: M must be 1..8");
-    int st = check_layout_dims(K, N, group);
-    if (st) return st;
-    if (K > 8 * kWarps * kGroup) return fail(MCV_ERR_SHAPE, "w4a16_gemv_silu_mul: K above 8192 unsupported");
-    if (!aligned16(qweight) || !aligned16(scales) || !aligned16(gate) || !aligned16(up))
-        return fail(MCV_ERR_ALIGN, "w4a16_gemv_silu_mul: gate, up, qweight and scales must be 16-byte aligned");
-    if (reinterpret_cast<uintptr_t>(zeros) & 3u) return fail(MCV_ERR_ALIGN, "w4a16_gemv_silu_mul: zeros must be 4-byte aligned");
-    if (zero_bias < 0 || zero_bias > 1) return fail(MCV_ERR_VALUE, "w4a16_gemv_silu_mul: zero_bias must be 0 or 1");
+int mcv_w4a16_gemv_gate_up_silu(const void* x, const mcv_w4a16_problem* gate, const mcv_w4a16_problem* up, void* act,
+                                int64_t M, mcv_stream_t stream) {
+    if (!x || !gate || !up || !act) return fail(MCV_ERR_NULL, "w4a16_gate_up_silu: null pointer");
+    if (M < 1 || M > 8) return fail(MCV_ERR_SHAPE, "w4a16_gate_up_silu: M must be 1..8");
+    const mcv_w4a16_problem* ps[2] = {gate, up};
+    for (const mcv_w4a16_problem* p : ps) {
+        if (!p->qweight || !p->scales || !p->zeros) return fail(MCV_ERR_NULL, "w4a16_gate_up_silu: null weight pointer");
+        int st = check_layout_dims(p->K, p->N, p->group);
+        if (st) return st;
+        if (!aligned16(p->qweight) || !aligned16(p->scales))
+            return fail(MCV_ERR_ALIGN, "w4a16_gate_up_silu: qweight and scales must be 16-byte aligned");
+        if (reinterpret_cast<uintptr_t>(p->zeros) & 3u) return fail(MCV_ERR_ALIGN, "w4a16_gate_up_silu: zeros must be 4-byte aligned");
+        if (p->zero_bias < 0 || p->zero_bias > 1) return fail(MCV_ERR_VALUE, "w4a16_gate_up_silu: zero_bias must be 0 or 1");
+    }
+    if (gate->K != up->K || gate->N != up->N) return fail(MCV_ERR_SHAPE, "w4a16_gate_up_silu: gate and up shapes differ");
+    if (gate->K > 32 * kGroup) return fail(MCV_ERR_SHAPE, "w4a16_gate_up_silu: K above 4096 unsupported");
+    if (!aligned16(x)) return fail(MCV_ERR_ALIGN, "w4a16_gate_up_silu: x must be 16-byte aligned");
     GroupParams gp{};
-    gp.count = 1;
-    gp.p[0] = Problem{static_cast<const __half*>(gate), static_cast<const uint4*>(qweight),
-                      static_cast<const __half*>(scales), static_cast<const uint32_t*>(zeros), static_cast<__half*>(out),
-                      static_cast<int>(K), static_cast<int>(N), zero_bias, 0};
+    gp.count = 2;
+    for (int i = 0; i < 2; ++i)
+        gp.p[i] = Problem{static_cast<const __half*>(x), static_cast<const uint4*>(ps[i]->qweight),
+                          static_cast<const __half*>(ps[i]->scales), static_cast<const uint32_t*>(ps[i]->zeros),
+                          static_cast<__half*>(act), ps[i]->K, ps[i]->N, ps[i]->zero_bias, 0};
     auto s = static_cast<cudaStream_t>(stream);
-    auto u = static_cast<const __half*>(up);
     switch (M) {
-        case 1: return launch_silu_m<1>(gp, u, s);
-        case 2: return launch_silu_m<2>(gp, u, s);
-        case 3: return launch_silu_m<3>(gp, u, s);
-        case 4: return launch_silu_m<4>(gp, u, s);
-        case 5: return launch_silu_m<5>(gp, u, s);
-        case 6: return launch_silu_m<6>(gp, u, s);
-        case 7: return launch_silu_m<7>(gp, u, s);
-        default: return launch_silu_m<8>(gp, u, s);
+        case 1: return launch_gate_up_m<1>(gp, s);
+        case 2: return launch_gate_up_m<2>(gp, s);
+        case 3: return launch_gate_up_m<3>(gp, s);
+        case 4: return launch_gate_up_m<4>(gp, s);
+        case 5: return launch_gate_up_m<5>(gp, s);
+        case 6: return launch_gate_up_m<6>(gp, s);
+        case 7: return launch_gate_up_m<7>(gp, s);
+        default: return launch_gate_up_m<8>(gp, s);
     }
 }
 

@@ -83,7 +83,7 @@ _SIGS = {
     "mcv_w4a16_safetensors_dims": [_vp, ctypes.c_char_p, _vp, _vp, _vp],
     "mcv_w4a16_load_safetensors": [_vp, ctypes.c_char_p, _vp, _vp, _vp, _vp, _vp],
     "mcv_w4a16_load_safetensors_host": [_vp, ctypes.c_char_p, _vp, _vp, _vp, _vp],
-    "mcv_w4a16_gemv_silu_mul": [_vp, _vp, _vp, _vp, _vp, _int, _vp, _i64, _i64, _i64, _i64, _vp],
+    "mcv_w4a16_gemv_gate_up_silu": [_vp, _vp, _vp, _vp, _i64, _vp],
     "mcv_w8a8_quantize": [_vp, _vp, _vp, _i64, _i64, _vp],
     "mcv_w8a8_gemm_i32": [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
     "mcv_w8a8_dequant": [_vp, _vp, _vp, _vp, _i64, _i64, _vp],
@@ -400,13 +400,18 @@ def matmul_w4a16(x, w: W4A16QuantizedWeight, out, stream=None) -> None:
                                 M, w.K, w.N, w.group_size, _stream(stream)), "matmul_w4a16")
 
 
-def matmul_w4a16_silu_mul(gate, up, w: W4A16QuantizedWeight, out, stream=None) -> None:
-    """out fp16 [M,N] = (silu(gate) * up) @ dequant(w): the down projection
-    with silu_mul fused into its activation load (mcv_w4a16_gemv_silu_mul)."""
-    M = gate.shape[0] if gate.dim() == 2 else 1
-    _check(lib().mcv_w4a16_gemv_silu_mul(_ptr(gate), _ptr(up), _ptr(w.qweight), _ptr(w.scales), _ptr(w.zeros),
-                                         w.zero_bias, _ptr(out), M, w.K, w.N, w.group_size, _stream(stream)),
-           "matmul_w4a16_silu_mul")
+def _problem(w: "W4A16QuantizedWeight"):
+    return W4A16Problem(None, _ptr(w.qweight), _ptr(w.scales), _ptr(w.zeros), None, w.K, w.N, w.group_size,
+                        w.zero_bias)
+
+
+def matmul_w4a16_gate_up_silu(x, w_gate: W4A16QuantizedWeight, w_up: W4A16QuantizedWeight, act, stream=None) -> None:
+    """act fp16 [M,N] = silu_mul(x @ dequant(w_gate), x @ dequant(w_up)) in one
+    launch (mcv_w4a16_gemv_gate_up_silu): the MLP's gate / up / silu_mul."""
+    M = x.shape[0] if x.dim() == 2 else 1
+    pg, pu = _problem(w_gate), _problem(w_up)
+    _check(lib().mcv_w4a16_gemv_gate_up_silu(_ptr(x), ctypes.byref(pg), ctypes.byref(pu), _ptr(act), M,
+                                             _stream(stream)), "matmul_w4a16_gate_up_silu")
 
 
 def matmul_w4a16_gemm(x, w: W4A16QuantizedWeight, out, stream=None) -> None:

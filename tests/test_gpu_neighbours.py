@@ -102,27 +102,32 @@ def test_lm_head_with_final_norm(cuda, M):
     assert np.array_equal(idx_host.numpy(), ref_idx)
 
 
-@pytest.mark.parametrize("M,K,N", [(1, 3584, 1024), (3, 3584, 1024), (8, 3584, 1024), (1, 1024, 3584),
-                                   (2, 8192, 256), (1, 384, 40)])
-def test_w4a16_down_with_silu_mul(cuda, M, K, N):
-    """Fused silu_mul + W4A16 GEMV == the two separate kernels (bit for bit)
-    and the oracle's silu_mul + GEMV (fp16 tolerance)."""
+@pytest.mark.parametrize("M,K,N", [(1, 1024, 3584), (3, 1024, 3584), (8, 1024, 3584), (1, 4096, 512),
+                                   (2, 384, 40), (1, 128, 8)])
+def test_gate_up_with_swiglu_epilogue(cuda, M, K, N):
+    """act = silu_mul(x . Wg, x . Wu) in one launch against the oracle's
+    W4A16 GEMVs, fp16 rounding of gate and up, then its silu_mul (fp16
+    tolerance), and against the separate GPU kernels (nearly every element
+    identical: only the fp32 summation order of the gate / up sums differs)."""
     import mcv_b200 as mcv
     torch = cuda
-    _, q, z, s = synth.w4a16_inputs(M, K, N, seed=K + N + M)
-    r = synth.rng(K * M)
-    gate = (r.standard_normal((M, K)) * 2).astype(np.float16)
-    up = r.standard_normal((M, K)).astype(np.float16)
-    w = mcv.pack_w4a16(q, z, s)
-    gd, ud = dev(torch, gate), dev(torch, up)
-    fused = torch.empty((M, N), dtype=torch.float16, device="cuda")
-    mcv.matmul_w4a16_silu_mul(gd, ud, w, fused)
-    act = torch.empty((M, K), dtype=torch.float16, device="cuda")
-    mcv.silu_mul(gd, ud, act)
+    x, qg, zg, sg = synth.w4a16_inputs(M, K, N, seed=K + N + M)
+    _, qu, zu, su = synth.w4a16_inputs(M, K, N, seed=K + N + M + 1)
+    wg, wu = mcv.pack_w4a16(qg, zg, sg), mcv.pack_w4a16(qu, zu, su)
+    xd = dev(torch, x)
+    act = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    mcv.matmul_w4a16_gate_up_silu(xd, wg, wu, act)
+    gate = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    up = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    mcv.matmul_w4a16(xd, wg, gate)
+    mcv.matmul_w4a16(xd, wu, up)
     two = torch.empty((M, N), dtype=torch.float16, device="cuda")
-    mcv.matmul_w4a16(act, w, two)
+    mcv.silu_mul(gate, up, two)
     torch.cuda.synchronize()
-    assert torch.equal(fused, two)
-    act_ref = oracle.silu_mul(gate, up)
-    ref = oracle.w4a16_gemv(act_ref, oracle.w4a16_fold_zeros(q, z), s, nthreads=8)
-    assert_f16_close(fused.cpu().numpy(), ref, what=f"silu+w4a16 M={M} K={K} N={N}")
+    got = act.cpu().numpy()
+    g_ref = oracle.f32_to_f16_rn(oracle.w4a16_gemv(x, oracle.w4a16_fold_zeros(qg, zg), sg, nthreads=8))
+    u_ref = oracle.f32_to_f16_rn(oracle.w4a16_gemv(x, oracle.w4a16_fold_zeros(qu, zu), su, nthreads=8))
+    ref = oracle.f16_to_f32(oracle.silu_mul(g_ref, u_ref))
+    assert_f16_close(got, ref, what=f"gate/up swiglu M={M} K={K} N={N}")
+    differ = np.count_nonzero(got.view(np.uint16) != two.cpu().numpy().view(np.uint16))
+    assert differ <= max(2, got.size // 50), differ

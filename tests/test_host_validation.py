@@ -82,11 +82,16 @@ def test_neighbour_arguments(L):
     assert L.mcv_silu_mul(F, F, None, 8, None) == NULL
     assert L.mcv_silu_mul(F2, F, F, 8, None) == ALIGN
     assert L.mcv_silu_mul(F, F, F, 0, None) == SHAPE
-    s = L.mcv_w4a16_gemv_silu_mul
-    assert s(F, F, F, F, F, 0, F, 9, 1024, 3584, 128, None) == SHAPE      # M
-    assert s(F, F, F, F, F, 0, F, 1, 16384, 3584, 128, None) == SHAPE     # K above 8192
-    assert s(F, None, F, F, F, 0, F, 1, 1024, 3584, 128, None) == NULL
-    assert s(F2, F, F, F, F, 0, F, 1, 1024, 3584, 128, None) == ALIGN
+    P = mcv_b200.W4A16Problem
+    good = P(None, F, F, F, None, 1024, 3584, 128, 0)
+    g = L.mcv_w4a16_gemv_gate_up_silu
+    assert g(F, ctypes.byref(good), None, F, 1, None) == NULL
+    assert g(F, ctypes.byref(good), ctypes.byref(good), F, 9, None) == SHAPE               # M
+    other = P(None, F, F, F, None, 1024, 1024, 128, 0)
+    assert g(F, ctypes.byref(good), ctypes.byref(other), F, 1, None) == SHAPE              # N differs
+    big = P(None, F, F, F, None, 8192, 3584, 128, 0)
+    assert g(F, ctypes.byref(big), ctypes.byref(big), F, 1, None) == SHAPE                 # K above 4096
+    assert g(F2, ctypes.byref(good), ctypes.byref(good), F, 1, None) == ALIGN
 
 
 def test_w8a8_arguments(L):
