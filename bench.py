@@ -532,6 +532,9 @@ def main():
     ap.add_argument("--profile", choices=["lm_head", "lm_head_w8a8", "w4a16", "w4a16_grouped", "w8a8", "gemm"],
                     help="run a few untimed launches of one kernel family (a small case for ncu)")
     ap.add_argument("--gemm-m", type=int, default=1024, help="--profile gemm: activation rows M")
+    ap.add_argument("--vocab", type=int, default=VOCAB,
+                    help="lm_head rows of the sharded headline step (default: the model's 248094); other values "
+                         "are studies, e.g. 8-GPU shard sizes on fewer GPUs, and are labelled so in the line")
     ap.add_argument("--rows", type=int, default=65536, help="--profile lm_head / lm_head_w8a8: vocab rows (65536 = 128 MB fp16)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -561,14 +564,15 @@ def main():
     # Every rank draws the same seeded full-vocabulary weight and keeps its
     # contiguous row range, so the sharded answer can be checked against the
     # CPU oracle over the whole vocabulary on rank 0.
-    per = (VOCAB + world - 1) // world
-    a, b = rank * per, min(VOCAB, (rank + 1) * per)
+    vocab = args.vocab
+    per = (vocab + world - 1) // world
+    a, b = rank * per, min(vocab, (rank + 1) * per)
     rows = b - a
     gen = torch.Generator(device="cuda")
     gen.manual_seed(1234)
     shard_bytes = rows * K_HIDDEN * 2
     copies = max(1, int(np.ceil(2 * l2 / shard_bytes)))
-    w_full = rand_f16(torch, (VOCAB, K_HIDDEN), 0.02, gen)
+    w_full = rand_f16(torch, (vocab, K_HIDDEN), 0.02, gen)
     x = rand_f16(torch, (1, K_HIDDEN), 1.0, gen)
     w_copies = [w_full[a:b].clone()]
     w_copies += [w_copies[0].clone() for _ in range(copies - 1)]
@@ -740,7 +744,8 @@ def main():
             "metric": METRIC, "value": round(us_step, 3), "unit": "us", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(us_step / 1e3, 6), "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded N(0,0.02) weights)",
-            "config": {"workload": WORKLOAD, "K": K_HIDDEN, "vocab": VOCAB, "M": 1, "shard_rows": rows,
+            "config": {"workload": WORKLOAD if vocab == VOCAB else f"lm_head study: vocab {vocab} (not the headline config)",
+                       "K": K_HIDDEN, "vocab": vocab, "M": 1, "shard_rows": rows,
                        "parallelism": f"vocab-shard x{world}" + (
                            " + NCCL allreduce(max) of uint64 keys" if comm is not None else
                            " + in-kernel peer-mailbox exchange of uint64 keys over NVLink" if p2p is not None else ""),
