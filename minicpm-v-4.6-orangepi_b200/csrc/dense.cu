@@ -456,6 +456,13 @@ int launch_rows_m(int kch, const Args& args, cudaStream_t s, int grid) {
                                                  static_cast<int>(smem));
             if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rows_kernel)");
         }
+        // a persistent grid: never more blocks than are resident at once
+        // (the wider-M variants use more than 64 registers, so fewer than 4
+        // of their blocks fit on an SM)
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kRowThreads, smem) == cudaSuccess &&
+            per_sm > 0 && grid > per_sm * sm_count())
+            grid = per_sm * sm_count();
         return launch(kern, dim3(grid), dim3(kRowThreads), smem, s, args);
     };
     switch (kch) {

@@ -35,25 +35,41 @@ __device__ __forceinline__ double warp_sum_f64(double v) {
 
 // Normalises M rows of H fp16 values (row stride H) from src into dst, with
 // all threads of the block (blockDim.x a multiple of 32, at most 1024).
-// src and dst may be global or shared memory, but must not overlap.  Ends
-// with a __syncthreads().
+// src and dst may be global or shared memory, but must not overlap.  When
+// H <= kNormCache * blockDim.x (e.g. a 1024-wide row on 256 threads) src is
+// read once and kept in registers between the two passes.  Ends with a
+// __syncthreads().
+constexpr int kNormCache = 4;
+
 template <int M>
 __device__ __forceinline__ void rms_norm_rows_block(const __half* src, __half* dst, int H, const NormArgs& na) {
     __shared__ double part[32][M];
     __shared__ float rstd_s[M];
     const int tid = threadIdx.x, nthr = blockDim.x;
     const int lane = tid & 31, warp = tid >> 5, nwarps = nthr >> 5;
+    const bool cached = H <= kNormCache * nthr;
+    float xc[kNormCache][M];
     double s[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) s[m] = 0.0;
-    for (int h = tid; h < H; h += nthr) {
+    auto sq = [&](float x) {
+        return na.variant == 0 ? static_cast<double>(__half2float(rn16(__fmul_rn(x, x))))
+                               : static_cast<double>(x) * static_cast<double>(x);
+    };
+    if (cached) {
 #pragma unroll
-        for (int m = 0; m < M; ++m) {
-            const float x = __half2float(src[static_cast<int64_t>(m) * H + h]);
-            if (na.variant == 0)
-                s[m] += static_cast<double>(__half2float(rn16(__fmul_rn(x, x))));
-            else
-                s[m] += static_cast<double>(x) * static_cast<double>(x);
+        for (int i = 0; i < kNormCache; ++i) {
+            const int h = tid + i * nthr;
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                xc[i][m] = h < H ? __half2float(src[static_cast<int64_t>(m) * H + h]) : 0.0f;
+                s[m] += sq(xc[i][m]);
+            }
+        }
+    } else {
+        for (int h = tid; h < H; h += nthr) {
+#pragma unroll
+            for (int m = 0; m < M; ++m) s[m] += sq(__half2float(src[static_cast<int64_t>(m) * H + h]));
         }
     }
 #pragma unroll
@@ -78,18 +94,28 @@ __device__ __forceinline__ void rms_norm_rows_block(const __half* src, __half* d
         rstd_s[m] = r;
     }
     __syncthreads();
-    for (int h = tid; h < H; h += nthr) {
+    auto put = [&](int h, int m, float x) {
         const float g = __half2float(na.gamma[h]);
-        const float gp1 = __half2float(rn16(__fadd_rn(g, 1.0f)));
+        __half o;
+        if (na.variant == 0)
+            o = rn16(__fmul_rn(__half2float(rn16(__fmul_rn(x, rstd_s[m]))), __half2float(rn16(__fadd_rn(g, 1.0f)))));
+        else
+            o = rn16(__fmul_rn(__fmul_rn(x, rstd_s[m]), g));
+        dst[static_cast<int64_t>(m) * H + h] = o;
+    };
+    if (cached) {
 #pragma unroll
-        for (int m = 0; m < M; ++m) {
-            const float x = __half2float(src[static_cast<int64_t>(m) * H + h]);
-            __half o;
-            if (na.variant == 0)
-                o = rn16(__fmul_rn(__half2float(rn16(__fmul_rn(x, rstd_s[m]))), gp1));
-            else
-                o = rn16(__fmul_rn(__fmul_rn(x, rstd_s[m]), g));
-            dst[static_cast<int64_t>(m) * H + h] = o;
+        for (int i = 0; i < kNormCache; ++i) {
+            const int h = tid + i * nthr;
+            if (h < H) {
+#pragma unroll
+                for (int m = 0; m < M; ++m) put(h, m, xc[i][m]);
+            }
+        }
+    } else {
+        for (int h = tid; h < H; h += nthr) {
+#pragma unroll
+            for (int m = 0; m < M; ++m) put(h, m, __half2float(src[static_cast<int64_t>(m) * H + h]));
         }
     }
     __syncthreads();

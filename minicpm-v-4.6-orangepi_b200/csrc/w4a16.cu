@@ -52,8 +52,8 @@ constexpr int kWarps = 8;
 constexpr int kBlocksPerSm = 2;
 constexpr int kMaxGroupProblems = 48;
 
-inline int64_t padded_n(int64_t N) { return (N + 15) / 16 * 16; }
-inline int64_t padded_g(int64_t G) { return (G + 7) / 8 * 8; }
+__host__ __device__ inline int64_t padded_n(int64_t N) { return (N + 15) / 16 * 16; }
+__host__ __device__ inline int64_t padded_g(int64_t G) { return (G + 7) / 8 * 8; }
 
 // An MMA's dot product does not depend on the order of k, so k is permuted
 // inside every 64-k quad, identically for weights and activations: lane
@@ -685,21 +685,23 @@ int run_group_wide(GroupParams& gp, int M, cudaStream_t st) {
 
 // The MLP's gate and up projections with SwiGLU in the epilogue
 // (decoder_layer.cpp:1186-1203): act = silu_mul(x . Wg, x . Wu).  Block b
-// computes strip b of both weights - warps 0-3 the gate, warps 4-7 the up
-// projection, each warp a quarter of the 128-k groups - so every lane ends
-// with the gate and up sums of the same (row, column) pairs.  Each is rounded
-// to fp16 (the projections' output type) and combined as the silu_mul kernel
-// does, so one launch replaces the grouped gate/up launch plus the silu_mul
+// computes strip b of both weights with 16 warps - warps 0-7 the gate, 8-15
+// the up projection, each half splitting K exactly as the K-split kernel does,
+// so the sums (and, after rounding to fp16, the projections' outputs) are the
+// separate GEMVs' bit for bit.  silu_mul's arithmetic then runs on the two
+// fp16 values, so one launch replaces the gate/up launch plus the silu_mul
 // launch, and the fp16 gate and up never travel through memory.
+constexpr int kGUWarps = 2 * kWarps;
+
 template <int M, int KG>
-__global__ void __launch_bounds__(kWarps * 32)
+__global__ void __launch_bounds__(kGUWarps * 32)
 w4a16_gate_up_silu_kernel(const __grid_constant__ GroupParams gp) {
-    __shared__ float4 red[kWarps][32];
+    __shared__ float4 red[kGUWarps][32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int strip = static_cast<int>(blockIdx.x);
-    const int wq = warp & 3;
-    const Problem& P = gp.p[warp >> 2];  // 0: gate, 1: up
+    const int wq = warp & (kWarps - 1);
+    const Problem& P = gp.p[warp / kWarps];  // 0: gate, 1: up
     const int K = P.K, G = K / kGroup, Gp = (G + 7) & ~7, zw = (G + 7) >> 3;
     const int col = strip * 16 + g;
     uint4 v[KG][2];
@@ -707,7 +709,7 @@ w4a16_gate_up_silu_kernel(const __grid_constant__ GroupParams gp) {
     int zlo[KG], zhi[KG];
 #pragma unroll
     for (int j = 0; j < KG; ++j) {
-        const int gi = wq + j * 4;
+        const int gi = wq + j * kWarps;
         v[j][0] = v[j][1] = make_uint4(0, 0, 0, 0);
         slo[j] = shi[j] = 0.0f;
         zlo[j] = zhi[j] = 0;
@@ -726,11 +728,11 @@ w4a16_gate_up_silu_kernel(const __grid_constant__ GroupParams gp) {
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int j = 0; j < KG; ++j) {
-        const int gi = wq + j * 4;
+        const int gi = wq + j * kWarps;
         if (gi >= G) break;
         float d[4];
-        group_mma<M, 1>(v[j], P.x + static_cast<size_t>(g) * K + gi * kGroup + 16 * t, g, zlo[j] + P.zero_bias,
-                        zhi[j] + P.zero_bias, d);
+        group_mma<M>(v[j], P.x + static_cast<size_t>(g) * K + gi * kGroup + 16 * t, g, zlo[j] + P.zero_bias,
+                     zhi[j] + P.zero_bias, d);
         acc[0] = fmaf(d[0], slo[j], acc[0]);
         acc[1] = fmaf(d[1], slo[j], acc[1]);
         acc[2] = fmaf(d[2], shi[j], acc[2]);
@@ -739,10 +741,10 @@ w4a16_gate_up_silu_kernel(const __grid_constant__ GroupParams gp) {
     red[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
     __syncthreads();
     if (warp == 0) {
-        float4 gs = red[0][lane], us = red[4][lane];
+        float4 gs = red[0][lane], us = red[kWarps][lane];
 #pragma unroll
-        for (int w = 1; w < 4; ++w) {
-            const float4 a = red[w][lane], b = red[4 + w][lane];
+        for (int w = 1; w < kWarps; ++w) {
+            const float4 a = red[w][lane], b = red[kWarps + w][lane];
             gs.x += a.x, gs.y += a.y, gs.z += a.z, gs.w += a.w;
             us.x += b.x, us.y += b.y, us.z += b.z, us.w += b.w;
         }
@@ -764,12 +766,11 @@ template <int M>
 int launch_gate_up_m(GroupParams& gp, cudaStream_t st) {
     const int strips = static_cast<int>(padded_n(gp.p[0].N) / 16);
     const int G = gp.p[0].K / kGroup;
-    const int per_warp = (G + 3) / 4;
-    auto go = [&](auto kern) { return launch(kern, dim3(strips), dim3(kWarps * 32), 0, st, gp); };
+    const int per_warp = (G + kWarps - 1) / kWarps;
+    auto go = [&](auto kern) { return launch(kern, dim3(strips), dim3(kGUWarps * 32), 0, st, gp); };
     if (per_warp <= 1) return go(w4a16_gate_up_silu_kernel<M, 1>);
     if (per_warp <= 2) return go(w4a16_gate_up_silu_kernel<M, 2>);
-    if (per_warp <= 4) return go(w4a16_gate_up_silu_kernel<M, 4>);
-    return go(w4a16_gate_up_silu_kernel<M, 8>);
+    return go(w4a16_gate_up_silu_kernel<M, 4>);
 }
 
 int assign_strips(GroupParams& gp) {

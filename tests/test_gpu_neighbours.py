@@ -107,8 +107,8 @@ def test_lm_head_with_final_norm(cuda, M):
 def test_gate_up_with_swiglu_epilogue(cuda, M, K, N):
     """act = silu_mul(x . Wg, x . Wu) in one launch against the oracle's
     W4A16 GEMVs, fp16 rounding of gate and up, then its silu_mul (fp16
-    tolerance), and against the separate GPU kernels (nearly every element
-    identical: only the fp32 summation order of the gate / up sums differs)."""
+    tolerance), and bit for bit against the separate GPU kernels (the fused
+    kernel splits K over its warps exactly as the single-GEMV kernel does)."""
     import mcv_b200 as mcv
     torch = cuda
     x, qg, zg, sg = synth.w4a16_inputs(M, K, N, seed=K + N + M)
@@ -129,5 +129,4 @@ def test_gate_up_with_swiglu_epilogue(cuda, M, K, N):
     u_ref = oracle.f32_to_f16_rn(oracle.w4a16_gemv(x, oracle.w4a16_fold_zeros(qu, zu), su, nthreads=8))
     ref = oracle.f16_to_f32(oracle.silu_mul(g_ref, u_ref))
     assert_f16_close(got, ref, what=f"gate/up swiglu M={M} K={K} N={N}")
-    differ = np.count_nonzero(got.view(np.uint16) != two.cpu().numpy().view(np.uint16))
-    assert differ <= max(2, got.size // 50), differ
+    assert np.array_equal(got.view(np.uint16), two.cpu().numpy().view(np.uint16))
