@@ -62,8 +62,7 @@ void mcv_set_pdl(int enabled);
  *   MCV_TUNE_W4A16_MODE: 1 = register-buffered streaming kernel (each warp
  *   owns whole 16-column strips), 2 = one block per strip with K split over
  *   its warps (K <= 8192), 3 = streaming kernel fed by warp-private
- *   bulk-copy rings, 4 = the same over pairs of adjacent strips (K a
- *   multiple of 256); default: K-split below 4 strips per SM, else 3.
+ *   bulk-copy rings; default: K-split below 4 strips per SM, else 3.
  *   MCV_TUNE_ROWS_BLOCKS_PER_SM: blocks per SM of the persistent lm_head /
  *   [N][K] GEMV grid (1..4; default 4 up to 600 rows per SM, else 2).
  *   MCV_TUNE_ROWS_PREFETCH: how many row steps ahead of its loads each warp

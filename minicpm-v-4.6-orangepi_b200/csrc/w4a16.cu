@@ -214,13 +214,11 @@ struct Problem {
     __half* out;
     int K, N, zero_bias;
     int strip_begin;   // first global strip index of this problem
-    int pair_begin;    // first global strip-pair index (pair kernel)
 };
 
 struct GroupParams {
     int count;
     int total_strips;
-    int total_pairs;
     Problem p[kMaxGroupProblems];
 };
 
@@ -471,134 +469,6 @@ w4a16_tma_kernel(const __grid_constant__ GroupParams gp) {
             next_item(gp, iss, W);
         }
         next_item(gp, cur, W);
-    }
-}
-
-// ---------------------------------------------------------------------------
-// Strip-pair streaming variant (MCV_TUNE_W4A16_MODE=4).  As the bulk-copy
-// kernel, but a ring item is two adjacent strips of one problem over 256 k
-// (two groups): the per-group activation loads, loop and ring bookkeeping
-// are shared by 32 weight columns instead of 16, and the stage keeps the
-// same 4 KB of weights (two 2 KB bulk copies) plus 32 columns' scales and
-// zero words.
-// ---------------------------------------------------------------------------
-constexpr int kPairK = 256;
-constexpr int kPairStageBytes = 4096 + 128 + 128;
-constexpr int kPairSmem = kWarps * kRing * kPairStageBytes + kWarps * kRing * 8;
-
-struct PairIter {
-    int pair, c, pi;
-};
-
-__device__ __forceinline__ int find_problem_pair(const GroupParams& gp, int pair, int start) {
-    int pi = start;
-    while (pi + 1 < gp.count && pair >= gp.p[pi + 1].pair_begin) ++pi;
-    return pi;
-}
-
-__device__ __forceinline__ void next_pair_item(const GroupParams& gp, PairIter& it, int W) {
-    if (++it.c == gp.p[it.pi].K / kPairK) {
-        it.c = 0;
-        it.pair += W;
-        if (it.pair < gp.total_pairs) it.pi = find_problem_pair(gp, it.pair, it.pi);
-    }
-}
-
-__device__ __forceinline__ void issue_pair_item(const GroupParams& gp, const PairIter& it, unsigned char* st,
-                                                uint64_t* bar, int lane) {
-    const Problem& P = gp.p[it.pi];
-    const int K = P.K, G = K / kGroup, Gp = (G + 7) & ~7, zw = (G + 7) >> 3;
-    const int strips = static_cast<int>(padded_n(P.N) / 16);
-    const int s0 = 2 * (it.pair - P.pair_begin);
-    const bool two = s0 + 1 < strips;
-    if (lane == 0) {
-        mbar_expect_tx(bar, two ? 4096u : 2048u);
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-            if (j == 0 || two)
-                bulk_load(st + j * 2048, P.qw + (static_cast<size_t>(s0 + j) * (K / 64) + it.c * 4) * 32, 2048u, bar);
-    }
-    if (lane < 16 || two) {
-        const int col = s0 * 16 + lane;
-        cp_async4(st + 4096 + lane * 4, P.s + static_cast<size_t>(col) * Gp + it.c * 2);
-        cp_async4(st + 4096 + 128 + lane * 4, P.z + static_cast<size_t>(col) * zw + (it.c >> 2));
-    }
-    cp_async_mbar_arrive(bar);
-}
-
-template <int M, int MATH>
-__global__ void __launch_bounds__(kWarps * 32, kTmaBlocksPerSm)
-w4a16_pair_kernel(const __grid_constant__ GroupParams gp) {
-    extern __shared__ __align__(128) unsigned char smem[];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int g = lane >> 2, t = lane & 3;
-    unsigned char* ring = smem + warp * kRing * kPairStageBytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * kRing * kPairStageBytes) + warp * kRing;
-    const int W = static_cast<int>(gridDim.x) * kWarps;
-    const int T = gp.total_pairs;
-    PairIter cur{warp * static_cast<int>(gridDim.x) + static_cast<int>(blockIdx.x), 0, 0};
-    if (cur.pair < T) cur.pi = find_problem_pair(gp, cur.pair, 0);
-    if (lane == 0)
-        for (int s = 0; s < kRing; ++s) mbar_init(&bars[s], 1 + 32);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    __syncwarp();
-    PairIter iss = cur;
-    for (int issued = 0; issued < kRing && iss.pair < T; ++issued) {
-        issue_pair_item(gp, iss, ring + issued * kPairStageBytes, &bars[issued], lane);
-        next_pair_item(gp, iss, W);
-    }
-    pdl_trigger();
-    pdl_wait();  // x may be the previous kernel's output
-    float acc[2][4] = {};
-#pragma unroll 1
-    for (int k = 0; cur.pair < T; ++k) {
-        const int s = k % kRing;
-        if (!mbar_wait(&bars[s], static_cast<uint32_t>(k / kRing) & 1u)) {
-            if (lane == 0) atomicOr(&g_w4a16_dev_error, kDevErrTimeout);
-            return;
-        }
-        const Problem& P = gp.p[cur.pi];
-        const int K = P.K;
-        const int strips = static_cast<int>(padded_n(P.N) / 16);
-        const int s0 = 2 * (cur.pair - P.pair_begin);
-        const bool two = s0 + 1 < strips;
-        const unsigned char* st = ring + s * kPairStageBytes;
-        const int zsh = 4 * ((2 * cur.c) & 7);
-#pragma unroll
-        for (int gi = 0; gi < 2; ++gi) {
-            const __half* xg = P.x + static_cast<size_t>(g) * K + cur.c * kPairK + gi * kGroup + 16 * t;
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                if (j == 1 && !two) break;
-                const unsigned char* sw = st + j * 2048;
-                const uint4 v[2] = {*reinterpret_cast<const uint4*>(sw + ((2 * gi) * 32 + lane) * 16),
-                                    *reinterpret_cast<const uint4*>(sw + ((2 * gi + 1) * 32 + lane) * 16)};
-                const uint32_t zlo = *reinterpret_cast<const uint32_t*>(st + 4096 + 128 + (j * 16 + g) * 4);
-                const uint32_t zhi = *reinterpret_cast<const uint32_t*>(st + 4096 + 128 + (j * 16 + g + 8) * 4);
-                const float s_lo = __half2float(*reinterpret_cast<const __half*>(st + 4096 + (j * 16 + g) * 4 + gi * 2));
-                const float s_hi = __half2float(*reinterpret_cast<const __half*>(st + 4096 + (j * 16 + g + 8) * 4 + gi * 2));
-                float d[4];
-                group_mma<M, MATH>(v, xg, g, static_cast<int>((zlo >> (zsh + 4 * gi)) & 0xfu) + P.zero_bias,
-                                   static_cast<int>((zhi >> (zsh + 4 * gi)) & 0xfu) + P.zero_bias, d);
-                acc[j][0] = fmaf(d[0], s_lo, acc[j][0]);
-                acc[j][1] = fmaf(d[1], s_lo, acc[j][1]);
-                acc[j][2] = fmaf(d[2], s_hi, acc[j][2]);
-                acc[j][3] = fmaf(d[3], s_hi, acc[j][3]);
-            }
-        }
-        if (cur.c + 1 == K / kPairK) {
-            store_strip<M>(P, s0, lane, acc[0]);
-            if (two) store_strip<M>(P, s0 + 1, lane, acc[1]);
-#pragma unroll
-            for (int j = 0; j < 2; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (iss.pair < T) {
-            issue_pair_item(gp, iss, ring + s * kPairStageBytes, &bars[s], lane);
-            next_pair_item(gp, iss, W);
-        }
-        next_pair_item(gp, cur, W);
     }
 }
 
@@ -904,16 +774,12 @@ int launch_gate_up_m(GroupParams& gp, cudaStream_t st) {
 }
 
 int assign_strips(GroupParams& gp) {
-    int t = 0, pr = 0;
+    int t = 0;
     for (int i = 0; i < gp.count; ++i) {
         gp.p[i].strip_begin = t;
-        gp.p[i].pair_begin = pr;
-        const int strips = static_cast<int>(padded_n(gp.p[i].N) / 16);
-        t += strips;
-        pr += (strips + 1) / 2;
+        t += static_cast<int>(padded_n(gp.p[i].N) / 16);
     }
     gp.total_strips = t;
-    gp.total_pairs = pr;
     return t;
 }
 
@@ -935,19 +801,6 @@ int launch_m(GroupParams& gp, cudaStream_t st) {
         if (per_warp <= 4) return go(w4a16_ksplit_kernel<M, 4, MATH>);
         if (per_warp <= 8) return go(w4a16_ksplit_kernel<M, 8, MATH>);
         // larger K: the streaming kernel has no K limit
-    }
-    if (mode == 4) {
-        bool k_ok = true;
-        for (int i = 0; i < gp.count; ++i) k_ok = k_ok && gp.p[i].K % kPairK == 0;
-        if (k_ok) {
-            auto kern = w4a16_pair_kernel<M, MATH>;
-            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem);
-            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a16_pair)");
-            int blocks = std::min((gp.total_pairs + kWarps - 1) / kWarps, sm_count() * kTmaBlocksPerSm);
-            const int t = tuning(MCV_TUNE_W4A16_GRID);
-            if (t > 0) blocks = std::min(t, sm_count() * kTmaBlocksPerSm);
-            return launch(kern, dim3(blocks), dim3(kWarps * 32), static_cast<size_t>(kPairSmem), st, gp);
-        }
     }
     if (mode == 1) {
         // register-buffered streaming kernel; at most kBlocksPerSm blocks per SM
