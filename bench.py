@@ -458,6 +458,51 @@ def bench_decode_step(torch, mcv, synth, hbm, lm_w, ws_lm):
     return res
 
 
+def bench_cpu_configs(synth):
+    """The CPU oracle (the reference tests' loops restated in C) on the other
+    configurations, single-threaded (the reference loop as written) and on all
+    host cores, so each GPU number has its CPU counterpart."""
+    import oracle
+    nthreads = os.cpu_count() or 1
+
+    def t(fn, reps):
+        fn()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        return (time.perf_counter() - t0) / reps * 1e6
+    res = {"cores": nthreads}
+    x, q, z, s = synth.w4a16_inputs(1, 1024, 3584, seed=0)
+    wz = oracle.w4a16_fold_zeros(q, z)
+    res["config0_w4a16_gemv"] = {"us_1_thread": round(t(lambda: oracle.w4a16_gemv(x, wz, s), 3), 1),
+                                 "us_all_cores": round(t(lambda: oracle.w4a16_gemv(x, wz, s, nthreads=nthreads), 10), 1)}
+    x8, w8, ws8 = synth.w8a8_inputs(1, 1024, 3584, seed=1)
+    res["config2_w8a8_M1_N3584"] = {"us_1_thread": round(t(lambda: oracle.w8a8_fused(x8, w8, ws8), 3), 1),
+                                    "us_all_cores": round(t(lambda: oracle.w8a8_fused(x8, w8, ws8, nthreads=nthreads), 10), 1)}
+    xg, qg, zg, sg = synth.w4a16_inputs(16, 1024, 4096, seed=2)
+    wg = oracle.w4a16_fold_zeros(qg, zg)
+    res["config4_w4a16_M16_N4096"] = {"us_1_thread": round(t(lambda: oracle.w4a16_gemv(xg, wg, sg), 1), 1),
+                                      "us_all_cores": round(t(lambda: oracle.w4a16_gemv(xg, wg, sg, nthreads=nthreads), 3), 1)}
+    # config 3: the 8 (linear-attention layer) and 7 (full-attention layer)
+    # projections timed once each, scaled to the 18 + 6 layers of a token
+    shapes = synth.decode_step_shapes()
+    per_layer = {}
+    for layer in (0, 3):
+        one = one_mt = 0.0
+        for (_, _, K, N) in [sh for sh in shapes if sh[0] == layer]:
+            xs, qs, zs, ss = synth.w4a16_inputs(1, K, N, seed=K + N)
+            wzs = oracle.w4a16_fold_zeros(qs, zs)
+            one += t(lambda: oracle.w4a16_gemv(xs, wzs, ss), 1)
+            one_mt += t(lambda: oracle.w4a16_gemv(xs, wzs, ss, nthreads=nthreads), 3)
+        per_layer[layer] = (one, one_mt)
+    res["config3_decode_matmuls_without_lm_head"] = {
+        "us_1_thread": round(18 * per_layer[0][0] + 6 * per_layer[3][0], 1),
+        "us_all_cores": round(18 * per_layer[0][1] + 6 * per_layer[3][1], 1),
+        "sample": "one linear-attention and one full-attention layer timed, scaled to 18 + 6 layers; "
+                  "add the lm_head's cpu_baseline for the whole step"}
+    return res
+
+
 def run_profile(args):
     """Untimed launches for an ncu capture: 2 warm-up + 3 profiled launches."""
     import torch
@@ -732,6 +777,7 @@ def main():
             extras["w4a16_gemm"] = bench_w4a16_gemm(torch, mcv, synth, l2, hbm, _tf)
             extras["gemm_f16"] = bench_gemm_f16(torch, mcv, l2, hbm, _tf)
             extras["lm_head_w8a8"] = bench_lm_head_w8a8(torch, mcv, hbm, w_copies[0])
+            extras["cpu_oracle_other_configs"] = bench_cpu_configs(synth)
 
     if rank == 0:
         algo_bytes = rows * K_HIDDEN * 2 + K_HIDDEN * 2 + 8
