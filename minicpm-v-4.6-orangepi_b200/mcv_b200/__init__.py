@@ -616,31 +616,41 @@ def silu_mul(gate, up, out, stream=None) -> None:
 
 class LmHeadGreedyStep:
     """A prepared mcv_lm_head_greedy_host call for a decode loop: tensors are
-    checked and their addresses resolved once, so each token costs one
-    library call (pass `w_shard` to switch weights between calls)."""
+    checked, their addresses resolved and every argument converted to its C
+    type once, so each token costs one library call with no per-call
+    argument conversion (pass `w_shard` to switch weights between calls)."""
+
+    _proto = ctypes.CFUNCTYPE(_int)
 
     def __init__(self, x_host, x_dev, w_shard, index_dev, index_host, workspace, ctx: "P2PContext" = None,
                  n_offset: int = 0, fp16_logits: bool = False, norm_gamma=None, norm_eps: float = 1e-6, stream=None):
         if x_host.is_cuda or index_host.is_cuda:
             raise RuntimeError("LmHeadGreedyStep: x_host and index_host live in host memory")
         M, K = x_host.shape
-        self._fn = lib().mcv_lm_head_greedy_host
+        # an unprototyped handle on the same entry point: the arguments below
+        # are already ctypes objects of the declared C types
+        self._fn = self._proto(ctypes.cast(lib().mcv_lm_head_greedy_host, _vp).value)
         self._shape = (M, K)
         self._rows = w_shard.shape[0]
-        self._head = (ctx.handle if ctx is not None else None, _vp(x_host.data_ptr()), _ptr(x_dev), _ptr(norm_gamma),
-                      norm_eps)
-        self._w = _ptr(w_shard)
-        self._tail = (_ptr(index_dev), _vp(index_host.data_ptr()), M, K)
-        self._rest = (n_offset, int(fp16_logits), _ptr(workspace), workspace.numel(), _stream(stream))
+        vp = lambda p: _vp(p if isinstance(p, int) else (p.value if p is not None else None))
+        self._head = (vp(ctx.handle if ctx is not None else None), _vp(x_host.data_ptr()), vp(_ptr(x_dev)),
+                      vp(_ptr(norm_gamma)), ctypes.c_float(norm_eps))
+        self._w = vp(_ptr(w_shard))
+        self._args = list(self._head) + [self._w, vp(_ptr(index_dev)), _vp(index_host.data_ptr()), _i64(M), _i64(K),
+                                         _i64(self._rows), _i64(n_offset), _int(int(fp16_logits)), vp(_ptr(workspace)),
+                                         _sz(workspace.numel()), vp(_stream(stream))]
         self._keep = (x_host, x_dev, w_shard, index_dev, index_host, workspace, norm_gamma)
 
     def __call__(self, w_shard=None) -> None:
-        w = self._w
+        args = self._args
         if w_shard is not None:
             if tuple(w_shard.shape) != (self._rows, self._shape[1]):
                 raise RuntimeError("LmHeadGreedyStep: weight shape differs from the prepared one")
-            w = _ptr(w_shard)
-        _check(self._fn(*self._head, w, *self._tail, self._rows, *self._rest), "lm_head_greedy_host")
+            args = list(args)
+            args[5] = _vp(w_shard.data_ptr())
+        st = self._fn(*args)
+        if st != 0:
+            _check(st, "lm_head_greedy_host")
 
 
 def w8a8_quantize(x, x_int8, x_scale, stream=None) -> None:
