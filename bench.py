@@ -543,6 +543,22 @@ def run_profile(args):
         out = torch.empty((args.gemm_m, 4096), dtype=torch.float16, device="cuda")
         for _ in range(5):
             mcv.matmul_w4a16_gemm(x, w, out)
+    elif args.profile == "gemm_f16":
+        x = torch.randn((args.gemm_m, 4096), device="cuda").to(torch.float16)
+        w = (torch.randn((4096, 4096), device="cuda") * 0.02).to(torch.float16)
+        out = torch.empty((args.gemm_m, 4096), dtype=torch.float16, device="cuda")
+        for _ in range(5):
+            mcv.gemm_f16(x, w, out)
+    elif args.profile == "gate_up":
+        # the MLP's gate / up / silu_mul in one launch, 24 layers' worth of weights
+        _, q, z, s = synth.w4a16_inputs(1, 1024, 3584, seed=0)
+        w0 = mcv.pack_w4a16(q, z, s)
+        ws = [mcv.W4A16QuantizedWeight(w0.qweight.clone(), w0.scales.clone(), w0.zeros.clone(), 0, 1024, 3584)
+              for _ in range(48)]
+        xd = torch.randn((1, 1024), device="cuda").to(torch.float16)
+        act = torch.empty((1, 3584), dtype=torch.float16, device="cuda")
+        for i in range(5):
+            mcv.matmul_w4a16_gate_up_silu(xd, ws[2 * i], ws[2 * i + 1], act)
     elif args.profile == "lm_head_w8a8":
         w = rand_f16(torch, (args.rows, K_HIDDEN), 0.02, gen)
         wq = torch.empty((args.rows, K_HIDDEN), dtype=torch.int8, device="cuda")
@@ -574,7 +590,8 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the config 0/2/3 sub-benchmarks")
     ap.add_argument("--collective", default="p2p", choices=["p2p", "nccl"],
                     help="N>1: fused peer-mailbox exchange inside the kernel, or a separate NCCL all-reduce")
-    ap.add_argument("--profile", choices=["lm_head", "lm_head_w8a8", "w4a16", "w4a16_grouped", "w8a8", "gemm"],
+    ap.add_argument("--profile", choices=["lm_head", "lm_head_w8a8", "w4a16", "w4a16_grouped", "w8a8", "gemm", "gemm_f16",
+                                          "gate_up"],
                     help="run a few untimed launches of one kernel family (a small case for ncu)")
     ap.add_argument("--gemm-m", type=int, default=1024, help="--profile gemm: activation rows M")
     ap.add_argument("--vocab", type=int, default=VOCAB,

@@ -405,6 +405,15 @@ int mcv_w8a8_gemm_i32(const void* x_int8, const void* w_int8, void* acc, int64_t
 int mcv_w8a8_dequant(const void* acc, const void* x_scale, const void* w_scale, void* out,
                      int64_t M, int64_t N, mcv_stream_t stream);
 
+/* matmul_decode_w8a8_prequant (src/csrc/lib/decoder_layer.cpp:216-224): the
+ * int32 GEMV of an already-quantized x (x_int8 [M][K], fp16 scales x_scale
+ * [M], from mcv_w8a8_quantize) with int8 [N][K] weights, then the dequant
+ * RN((acc * w_scale) * x_scale), in one kernel - so one quantization of the
+ * MLP input serves both the gate and the up projection, as in
+ * decoder_layer.cpp:1186-1197.  acc_out (int32 [M][N]) is optional. */
+int mcv_w8a8_gemv_prequant(const void* x_int8, const void* x_scale, const void* w_int8, const void* w_scale, void* out,
+                           void* acc_out, int64_t M, int64_t K, int64_t N, mcv_stream_t stream);
+
 /* Quantize + int8 GEMM + dequant in one kernel (w_layout 0) or three
  * (w_layout 1).  acc_out (int32 [M][N]), x_int8_out and x_scale_out are
  * optional copies of the intermediates (may be NULL).

@@ -163,6 +163,20 @@ void w8a8_dequant(const T& acc, const T& x_scale, const T& w_scale, T& out, cuda
     finish(stream, sync, "w8a8_dequant");
 }
 
+/* matmul_decode_w8a8_prequant (decoder_layer.cpp:216-224): int8 x with its
+ * fp16 scales (from w8a8_quantize) against a W8A8Weight, int32 GEMV + dequant
+ * in one kernel. */
+template <class T>
+void matmul_decode_w8a8_prequant(const T& x_int8, const T& x_scale, const W8A8Weight& w, T& out, cudaStream_t stream,
+                                 bool sync = false) {
+    detail::need_rank2(x_int8, "matmul_decode_w8a8_prequant");
+    if (x_int8.shape()[1] != w.K) throw Error(MCV_ERR_SHAPE, "matmul_decode_w8a8_prequant: x and weight K differ");
+    check(mcv_w8a8_gemv_prequant(x_int8.data(), x_scale.data(), w.w_int8, w.w_scale, out.data(), nullptr,
+                                 x_int8.shape()[0], w.K, w.N, stream),
+          "matmul_decode_w8a8_prequant");
+    finish(stream, sync, "matmul_decode_w8a8_prequant");
+}
+
 /* The projection's format chosen like matmul_decode_dispatch
  * (decoder_layer.cpp:226-244); absent formats are nullptr. */
 template <class T>

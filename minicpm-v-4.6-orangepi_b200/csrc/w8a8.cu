@@ -69,6 +69,7 @@ struct W8Args {
     int32_t* acc;           // [M][N] (optional when FUSED)
     int8_t* xq_out;         // [M][K] (optional, FUSED, written by block 0)
     __half* xs_out;         // [M]    (optional, FUSED, written by block 0)
+    const __half* xs_in;    // [M] scales of an int8 x (not FUSED): with w_scale and out, dequantize in the epilogue
     int K;
     int N;
 };
@@ -104,7 +105,7 @@ w8_rows_kernel(W8Args a) {
             wv[j][i] = make_uint4(0, 0, 0, 0);
             if (n < a.N && c < chunks) wv[j][i] = ld_stream(a.w + static_cast<int64_t>(n) * a.K + c * 16);
         }
-        if constexpr (FUSED) {
+        if (FUSED || a.xs_in) {
             if (n < a.N) wsc[j] = __half2float(a.w_scale[n]);
         }
     }
@@ -117,6 +118,7 @@ w8_rows_kernel(W8Args a) {
     } else {
         const uint4* src = static_cast<const uint4*>(a.x);
         for (int idx = threadIdx.x; idx < M * chunks; idx += kW8Warps * 32) xq_s[idx] = src[idx];
+        if (a.xs_in && threadIdx.x < M) xscale_s[threadIdx.x] = __half2float(a.xs_in[threadIdx.x]);
     }
     __syncthreads();
 
@@ -155,7 +157,7 @@ w8_rows_kernel(W8Args a) {
             if (lane == ((j * M + m) & 31) && n < a.N) {
                 const int64_t o = static_cast<int64_t>(m) * a.N + n;
                 if (a.acc) a.acc[o] = v;
-                if constexpr (FUSED) {
+                if (FUSED || a.xs_in) {
                     const float d = __fmul_rn(__fmul_rn(__int2float_rn(v), wsc[j]), xscale_s[m]);
                     a.out[o] = __float2half_rn(d);
                 }
@@ -208,7 +210,7 @@ w8_mma_kernel(W8Args a) {
         }
     }
     float wsc_lo = 0.0f, wsc_hi = 0.0f;
-    if constexpr (FUSED) {
+    if (FUSED || a.xs_in) {
         if (lo_ok) wsc_lo = __half2float(a.w_scale[n0 + g]);
         if (hi_ok) wsc_hi = __half2float(a.w_scale[n0 + g + 8]);
     }
@@ -225,6 +227,7 @@ w8_mma_kernel(W8Args a) {
             const int m = idx / cpr, c = idx - m * cpr;
             *reinterpret_cast<uint4*>(xq8 + m * stride + c * 16) = src[idx];
         }
+        if (a.xs_in && threadIdx.x < M) xscale_s[threadIdx.x] = __half2float(a.xs_in[threadIdx.x]);
     }
     __syncthreads();
 
@@ -257,7 +260,7 @@ w8_mma_kernel(W8Args a) {
             if (m >= M || n >= a.N) continue;
             const int64_t o = static_cast<int64_t>(m) * a.N + n;
             if (a.acc) a.acc[o] = vals[e];
-            if constexpr (FUSED) {
+            if (FUSED || a.xs_in) {
                 const float wsc = (e >> 1) ? wsc_hi : wsc_lo;
                 a.out[o] = __float2half_rn(__fmul_rn(__fmul_rn(__int2float_rn(vals[e]), wsc), xscale_s[m]));
             }
@@ -581,6 +584,25 @@ int mcv_w8a8_fused(const void* x, const void* w_int8, const void* w_scale, void*
     st = mcv_w8a8_gemm_i32(x_int8_out, w_int8, acc_out, M, K, N, 1, stream);
     if (st) return st;
     return launch_dequant(acc_out, x_scale_out, w_scale, out, M, N, s);
+}
+
+int mcv_w8a8_gemv_prequant(const void* x_int8, const void* x_scale, const void* w_int8, const void* w_scale, void* out,
+                           void* acc_out, int64_t M, int64_t K, int64_t N, mcv_stream_t stream) {
+    if (!x_int8 || !x_scale || !w_int8 || !w_scale || !out) return fail(MCV_ERR_NULL, "w8a8_gemv_prequant: null pointer");
+    int st = check_mkn(M, K, N);
+    if (st) return st;
+    if (!aligned16(w_int8) || !aligned16(x_int8))
+        return fail(MCV_ERR_ALIGN, "w8a8_gemv_prequant: x_int8 and w must be 16-byte aligned");
+    W8Args a{};
+    a.x = x_int8;
+    a.w = static_cast<const int8_t*>(w_int8);
+    a.w_scale = static_cast<const __half*>(w_scale);
+    a.xs_in = static_cast<const __half*>(x_scale);
+    a.out = static_cast<__half*>(out);
+    a.acc = static_cast<int32_t*>(acc_out);
+    a.K = static_cast<int>(K);
+    a.N = static_cast<int>(N);
+    return launch_w8_rows<false>(M, a, static_cast<cudaStream_t>(stream));
 }
 
 int mcv_w8a8_quantize_weight(const void* w_kn, void* wq, void* w_scale, int64_t K, int64_t N, int w_layout,

@@ -87,6 +87,7 @@ _SIGS = {
     "mcv_w8a8_quantize": [_vp, _vp, _vp, _i64, _i64, _vp],
     "mcv_w8a8_gemm_i32": [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
     "mcv_w8a8_dequant": [_vp, _vp, _vp, _vp, _i64, _i64, _vp],
+    "mcv_w8a8_gemv_prequant": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "mcv_w8a8_fused": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
     "mcv_w8a8_quantize_weight": [_vp, _vp, _vp, _i64, _i64, _int, _vp],
     "mcv_lm_head_argmax_w8a8": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _sz, _vp],
@@ -670,6 +671,15 @@ def w8a8_dequant(acc, x_scale, w_scale, out, stream=None) -> None:
     M, N = acc.shape
     _check(lib().mcv_w8a8_dequant(_ptr(acc), _ptr(x_scale), _ptr(w_scale), _ptr(out), M, N, _stream(stream)),
            "w8a8_dequant")
+
+
+def matmul_decode_w8a8_prequant(x_int8, x_scale, w_int8, w_scale, out, acc=None, stream=None) -> None:
+    """out fp16 [M,N] from an already-quantized x (w8a8_quantize) and int8
+    [N,K] weights: int32 GEMV + dequant in one kernel (mcv_w8a8_gemv_prequant)."""
+    M, K = x_int8.shape
+    N = w_int8.shape[0]
+    _check(lib().mcv_w8a8_gemv_prequant(_ptr(x_int8), _ptr(x_scale), _ptr(w_int8), _ptr(w_scale), _ptr(out), _ptr(acc),
+                                        M, K, N, _stream(stream)), "matmul_decode_w8a8_prequant")
 
 
 def w8a8_fused(x, w_int8, w_scale, out, acc=None, x_int8=None, x_scale=None, w_layout: int = 0,

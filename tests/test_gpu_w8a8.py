@@ -177,3 +177,29 @@ def test_gpu_weight_quantizer_equals_reference_code_output(cuda):
     torch.cuda.synchronize()
     assert np.array_equal(wq.cpu().numpy(), ref_wq)
     assert np.array_equal(ws.cpu().numpy().view(np.uint16), ref_ws)
+
+
+@pytest.mark.parametrize("M,N", [(1, 3584), (4, 1024), (8, 3584)])
+def test_prequant_gemv_equals_fused(cuda, M, N):
+    """matmul_decode_w8a8_prequant: quantize once, then int32 GEMV + dequant in
+    one kernel; bit-exact against the oracle and the one-kernel fused path."""
+    import mcv_b200 as mcv
+    torch = cuda
+    x, w, ws = synth.w8a8_inputs(M, 1024, N, seed=M * 7 + N)
+    xd = torch.from_numpy(x).cuda()
+    wt = torch.from_numpy(np.ascontiguousarray(w.T)).cuda()
+    wsd = torch.from_numpy(ws).cuda()
+    xq = torch.empty((M, 1024), dtype=torch.int8, device="cuda")
+    xs = torch.empty(M, dtype=torch.float16, device="cuda")
+    mcv.w8a8_quantize(xd, xq, xs)
+    out = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    acc = torch.empty((M, N), dtype=torch.int32, device="cuda")
+    for kernel in (1, 2):  # DP4A and the integer tensor cores
+        mcv.set_tuning(6, kernel)
+        out.fill_(0)
+        mcv.matmul_decode_w8a8_prequant(xq, xs, wt, wsd, out, acc=acc)
+        torch.cuda.synchronize()
+        r_acc, r_out = oracle.w8a8_fused(x, w, ws)
+        assert np.array_equal(acc.cpu().numpy(), np.asarray(r_acc).reshape(M, N))
+        assert np.array_equal(out.cpu().numpy().view(np.uint16), np.asarray(r_out).reshape(M, N))
+    mcv.set_tuning(6, 0)

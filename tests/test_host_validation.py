@@ -102,6 +102,9 @@ def test_w8a8_arguments(L):
     assert L.mcv_w8a8_fused(F2, F, F, F, None, None, None, 1, 1024, 3584, 0, None) == ALIGN
     assert L.mcv_w8a8_fused(None, F, F, F, None, None, None, 1, 1024, 3584, 0, None) == NULL
     assert L.mcv_w8a8_quantize(F, F, F, 0, 1024, None) == SHAPE
+    assert L.mcv_w8a8_gemv_prequant(F, None, F, F, F, None, 1, 1024, 3584, None) == NULL
+    assert L.mcv_w8a8_gemv_prequant(F, F, F, F, F, None, 9, 1024, 3584, None) == SHAPE
+    assert L.mcv_w8a8_gemv_prequant(F2, F, F, F, F, None, 1, 1024, 3584, None) == ALIGN
     assert L.mcv_w8a8_quantize_weight(F, F, F, 1024, 3584, 3, None) == VALUE
 
 
