@@ -245,7 +245,37 @@ def bench_w8a8(torch, mcv, synth, l2, hbm):
             res.append({"M": M, "N": N, "us": round(us, 4), "GBps": round(gbs, 1),
                         "frac_of_hbm": round(gbs / hbm, 4)})
             del wts, g
-    return {"config": "config2 fused quantize+int8 GEMV+dequant, K=1024, weights [N][K]", "cases": res}
+    # independent GEMVs, 16 per grouped launch (throughput, as for W4A16)
+    grouped = []
+    for M in (1, 8):
+        N = 3584
+        x, w, wsc = synth.w8a8_inputs(M, K, N, seed=M * 10 + N)
+        wt = torch.from_numpy(np.ascontiguousarray(w.T)).cuda()
+        copies = max(16, int(np.ceil(2 * l2 / wt.numel() / 16)) * 16)
+        wts = [wt] + [wt.clone() for _ in range(copies - 1)]
+        xd = torch.from_numpy(x).cuda()
+        sd = torch.from_numpy(wsc).cuda()
+        outs = [torch.empty((M, N), dtype=torch.float16, device="cuda") for _ in range(copies)]
+        probs = [mcv.w8a8_problems([(xd, t, sd, o) for t, o in zip(wts[i:i + 16], outs[i:i + 16])])
+                 for i in range(0, copies, 16)]
+
+        def gstep():
+            for p in probs:
+                mcv.w8a8_fused_grouped(problems=p, M=M, K=K)
+        gstep()
+        torch.cuda.synchronize()
+        g = graph_of(torch, gstep, torch.cuda.Stream())
+        g.replay()
+        torch.cuda.synchronize()
+        us = time_graph_ms(torch, g, reps=10) / copies * 1e3
+        byts = K * N + N * 2 + M * K * 2 + M * N * 2
+        gbs = byts / (us * 1e-6) / 1e9
+        grouped.append({"M": M, "N": N, "us_per_gemv": round(us, 4), "GBps": round(gbs, 1),
+                        "frac_of_hbm": round(gbs / hbm, 4), "gemvs_per_launch": 16})
+        del wts, g
+    return {"config": "config2 fused quantize+int8 GEMV+dequant, K=1024, weights [N][K]", "cases": res,
+            "grouped": grouped,
+            "timing": "cases: one dependent launch per GEMV; grouped: 16 independent GEMVs per launch"}
 
 
 def bench_w4a16_gemm(torch, mcv, synth, l2, hbm, tflops):

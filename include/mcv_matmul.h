@@ -414,6 +414,19 @@ int mcv_w8a8_dequant(const void* acc, const void* x_scale, const void* w_scale, 
 int mcv_w8a8_gemv_prequant(const void* x_int8, const void* x_scale, const void* w_int8, const void* w_scale, void* out,
                            void* acc_out, int64_t M, int64_t K, int64_t N, mcv_stream_t stream);
 
+/* Independent fused W8A8 GEMVs in one launch, e.g. the gate and up
+ * projections on the same input (decoder_layer.cpp:1186-1197) or a batch of
+ * unrelated ones: each problem is mcv_w8a8_fused with w_layout 0 (int8
+ * [N][K] weights); all share M (1..8) and K; at most 16 problems. */
+typedef struct mcv_w8a8_problem {
+    const void* x;       /* fp16 [M][K] */
+    const void* w_int8;  /* int8 [N][K] */
+    const void* w_scale; /* fp16 [N] */
+    void* out;           /* fp16 [M][N] */
+    int64_t N;
+} mcv_w8a8_problem;
+int mcv_w8a8_fused_grouped(const mcv_w8a8_problem* problems, int count, int64_t M, int64_t K, mcv_stream_t stream);
+
 /* Quantize + int8 GEMM + dequant in one kernel (w_layout 0) or three
  * (w_layout 1).  acc_out (int32 [M][N]), x_int8_out and x_scale_out are
  * optional copies of the intermediates (may be NULL).

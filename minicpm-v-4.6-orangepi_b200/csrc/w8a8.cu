@@ -74,6 +74,21 @@ struct W8Args {
     int N;
 };
 
+// Independent GEMVs of one launch (same K and M): problem i owns blocks
+// [block_begin[i], block_begin[i + 1]).  A single GEMV is a group of one.
+constexpr int kW8MaxProblems = 16;
+struct W8Group {
+    int count;
+    int block_begin[kW8MaxProblems + 1];
+    W8Args p[kW8MaxProblems];
+};
+
+__device__ __forceinline__ int w8_problem_of(const W8Group& gr, int block) {
+    int pi = 0;
+    while (pi + 1 < gr.count && block >= gr.block_begin[pi + 1]) ++pi;
+    return pi;
+}
+
 // Fused prologue: quantizes the M activation rows of a.x into xq8 (row
 // stride `stride` bytes) and their fp16-rounded scales into xscale_s, per
 // row exactly as w8a8_quantize; block 0 also writes the optional copies.
@@ -85,12 +100,15 @@ __device__ __forceinline__ void fused_quantize_x(const W8Args& a, int8_t* xq8, i
 
 template <int M, int KCH, bool FUSED>
 __global__ void __launch_bounds__(kW8Warps * 32)
-w8_rows_kernel(W8Args a) {
+w8_rows_kernel(const __grid_constant__ W8Group gr) {
     extern __shared__ uint4 xq_s[];  // int8 x as [M][K/16] 16-byte chunks
     __shared__ float xscale_s[M];
+    const int pi = w8_problem_of(gr, static_cast<int>(blockIdx.x));
+    const W8Args& a = gr.p[pi];
+    const int bid = static_cast<int>(blockIdx.x) - gr.block_begin[pi];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
-    const int n0 = (blockIdx.x * kW8Warps + warp) * kW8Cpw;
+    const int n0 = (bid * kW8Warps + warp) * kW8Cpw;
     const int chunks = a.K >> 4;
 
     uint4 wv[kW8Cpw][KCH];
@@ -187,13 +205,15 @@ __device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, ui
 
 template <int M, int KB, bool FUSED>
 __global__ void __launch_bounds__(kW8Warps * 32)
-w8_mma_kernel(W8Args a) {
+w8_mma_kernel(const __grid_constant__ W8Group gr) {
     extern __shared__ uint4 xq_s[];  // int8 x, M rows of K + kXqPad bytes
     __shared__ float xscale_s[M];
     __shared__ int4 red[kW8Warps][32];
+    const int pi = w8_problem_of(gr, static_cast<int>(blockIdx.x));
+    const W8Args& a = gr.p[pi];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int n0 = blockIdx.x * 16;
+    const int n0 = (static_cast<int>(blockIdx.x) - gr.block_begin[pi]) * 16;
     const int K = a.K, nkb = (K + 63) / 64, stride = K + kXqPad;
     const bool lo_ok = n0 + g < a.N, hi_ok = n0 + g + 8 < a.N;
 
@@ -410,11 +430,23 @@ __global__ void quantize_weight_kernel(const __half* __restrict__ w, int8_t* __r
     }
 }
 
+// Fills the group's block ranges for blocks of `cols` output columns.
+int w8_assign_blocks(W8Group& gr, int cols) {
+    int b = 0;
+    for (int i = 0; i < gr.count; ++i) {
+        gr.block_begin[i] = b;
+        b += (gr.p[i].N + cols - 1) / cols;
+    }
+    gr.block_begin[gr.count] = b;
+    return b;
+}
+
 template <int M, bool FUSED>
-int launch_w8_mma_m(const W8Args& a, cudaStream_t s) {
+int launch_w8_mma_m(W8Group& gr, cudaStream_t s) {
+    const W8Args& a = gr.p[0];
     const int nkb = (a.K + 63) / 64;
     const int per_warp = (nkb + kW8Warps - 1) / kW8Warps;
-    const dim3 grid((a.N + 15) / 16);
+    const dim3 grid(w8_assign_blocks(gr, 16));
     const dim3 block(kW8Warps * 32);
     const size_t smem = static_cast<size_t>(M) * (a.K + kXqPad);
     auto go = [&](auto kern) -> int {
@@ -422,7 +454,7 @@ int launch_w8_mma_m(const W8Args& a, cudaStream_t s) {
             cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
             if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w8_mma)");
         }
-        return launch(kern, grid, block, smem, s, a);
+        return launch(kern, grid, block, smem, s, gr);
     };
     if (per_warp <= 1) return go(w8_mma_kernel<M, 1, FUSED>);
     if (per_warp <= 2) return go(w8_mma_kernel<M, 2, FUSED>);
@@ -432,15 +464,16 @@ int launch_w8_mma_m(const W8Args& a, cudaStream_t s) {
 }
 
 template <int M, bool FUSED>
-int launch_w8_rows_m(const W8Args& a, cudaStream_t s) {
+int launch_w8_rows_m(W8Group& gr, cudaStream_t s) {
     // one activation row: DP4A is quicker (1.93 vs 2.18 us at N=3584); from
     // four rows the tensor cores are (2.73 vs 4.05 us at M=4, N=3584), B200
     const int t = tuning(MCV_TUNE_W8A8_KERNEL);
-    if (t == 2 || (t != 1 && M >= 2)) return launch_w8_mma_m<M, FUSED>(a, s);
+    if (t == 2 || (t != 1 && M >= 2)) return launch_w8_mma_m<M, FUSED>(gr, s);
+    const W8Args& a = gr.p[0];
     const int chunks_per_lane = (a.K / 16 + 31) / 32;
     int kch = 1;
     while (kch < chunks_per_lane) kch *= 2;
-    const dim3 grid((a.N + kW8Warps * kW8Cpw - 1) / (kW8Warps * kW8Cpw));
+    const dim3 grid(w8_assign_blocks(gr, kW8Warps * kW8Cpw));
     const dim3 block(kW8Warps * 32);
     const size_t smem = static_cast<size_t>(M) * a.K;
     auto go = [&](auto kern) -> int {
@@ -448,7 +481,7 @@ int launch_w8_rows_m(const W8Args& a, cudaStream_t s) {
             cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
             if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w8_rows)");
         }
-        return launch(kern, grid, block, smem, s, a);
+        return launch(kern, grid, block, smem, s, gr);
     };
     switch (kch) {
         case 1: return go(w8_rows_kernel<M, 1, FUSED>);
@@ -460,17 +493,25 @@ int launch_w8_rows_m(const W8Args& a, cudaStream_t s) {
 }
 
 template <bool FUSED>
-int launch_w8_rows(int64_t M, const W8Args& a, cudaStream_t s) {
+int launch_w8_group(int64_t M, W8Group& gr, cudaStream_t s) {
     switch (M) {
-        case 1: return launch_w8_rows_m<1, FUSED>(a, s);
-        case 2: return launch_w8_rows_m<2, FUSED>(a, s);
-        case 3: return launch_w8_rows_m<3, FUSED>(a, s);
-        case 4: return launch_w8_rows_m<4, FUSED>(a, s);
-        case 5: return launch_w8_rows_m<5, FUSED>(a, s);
-        case 6: return launch_w8_rows_m<6, FUSED>(a, s);
-        case 7: return launch_w8_rows_m<7, FUSED>(a, s);
-        default: return launch_w8_rows_m<8, FUSED>(a, s);
+        case 1: return launch_w8_rows_m<1, FUSED>(gr, s);
+        case 2: return launch_w8_rows_m<2, FUSED>(gr, s);
+        case 3: return launch_w8_rows_m<3, FUSED>(gr, s);
+        case 4: return launch_w8_rows_m<4, FUSED>(gr, s);
+        case 5: return launch_w8_rows_m<5, FUSED>(gr, s);
+        case 6: return launch_w8_rows_m<6, FUSED>(gr, s);
+        case 7: return launch_w8_rows_m<7, FUSED>(gr, s);
+        default: return launch_w8_rows_m<8, FUSED>(gr, s);
     }
+}
+
+template <bool FUSED>
+int launch_w8_rows(int64_t M, const W8Args& a, cudaStream_t s) {
+    W8Group gr{};
+    gr.count = 1;
+    gr.p[0] = a;
+    return launch_w8_group<FUSED>(M, gr, s);
 }
 
 int launch_w8_kn(int64_t M, const int8_t* xq, const int8_t* w, int32_t* acc, int K, int N, cudaStream_t s) {
@@ -603,6 +644,29 @@ int mcv_w8a8_gemv_prequant(const void* x_int8, const void* x_scale, const void* 
     a.K = static_cast<int>(K);
     a.N = static_cast<int>(N);
     return launch_w8_rows<false>(M, a, static_cast<cudaStream_t>(stream));
+}
+
+int mcv_w8a8_fused_grouped(const mcv_w8a8_problem* problems, int count, int64_t M, int64_t K, mcv_stream_t stream) {
+    if (!problems || count < 1) return fail(MCV_ERR_NULL, "w8a8_fused_grouped: no problems");
+    if (count > kW8MaxProblems) return fail(MCV_ERR_SHAPE, "w8a8_fused_grouped: at most 16 problems per launch");
+    int st = check_mkn(M, K, 16);
+    if (st) return st;
+    W8Group gr{};
+    gr.count = count;
+    for (int i = 0; i < count; ++i) {
+        const mcv_w8a8_problem& q = problems[i];
+        if (!q.x || !q.w_int8 || !q.w_scale || !q.out) return fail(MCV_ERR_NULL, "w8a8_fused_grouped: null pointer");
+        if (q.N < 1 || q.N > (1 << 30)) return fail(MCV_ERR_SHAPE, "w8a8_fused_grouped: bad N");
+        if (!aligned16(q.x) || !aligned16(q.w_int8)) return fail(MCV_ERR_ALIGN, "w8a8_fused_grouped: x and w must be 16-byte aligned");
+        W8Args& a = gr.p[i];
+        a.x = q.x;
+        a.w = static_cast<const int8_t*>(q.w_int8);
+        a.w_scale = static_cast<const __half*>(q.w_scale);
+        a.out = static_cast<__half*>(q.out);
+        a.K = static_cast<int>(K);
+        a.N = static_cast<int>(q.N);
+    }
+    return launch_w8_group<true>(M, gr, static_cast<cudaStream_t>(stream));
 }
 
 int mcv_w8a8_quantize_weight(const void* w_kn, void* wq, void* w_scale, int64_t K, int64_t N, int w_layout,

@@ -88,6 +88,7 @@ _SIGS = {
     "mcv_w8a8_gemm_i32": [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
     "mcv_w8a8_dequant": [_vp, _vp, _vp, _vp, _i64, _i64, _vp],
     "mcv_w8a8_gemv_prequant": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "mcv_w8a8_fused_grouped": [_vp, _int, _i64, _i64, _vp],
     "mcv_w8a8_fused": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
     "mcv_w8a8_quantize_weight": [_vp, _vp, _vp, _i64, _i64, _int, _vp],
     "mcv_lm_head_argmax_w8a8": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _sz, _vp],
@@ -680,6 +681,28 @@ def matmul_decode_w8a8_prequant(x_int8, x_scale, w_int8, w_scale, out, acc=None,
     N = w_int8.shape[0]
     _check(lib().mcv_w8a8_gemv_prequant(_ptr(x_int8), _ptr(x_scale), _ptr(w_int8), _ptr(w_scale), _ptr(out), _ptr(acc),
                                         M, K, N, _stream(stream)), "matmul_decode_w8a8_prequant")
+
+
+class W8A8Problem(ctypes.Structure):
+    """One GEMV of mcv_w8a8_fused_grouped."""
+    _fields_ = [("x", _vp), ("w_int8", _vp), ("w_scale", _vp), ("out", _vp), ("N", _i64)]
+
+
+def w8a8_problems(items):
+    """[(x fp16 [M,K], w_int8 [N,K], w_scale [N], out [M,N]), ...] -> ctypes array."""
+    arr = (W8A8Problem * len(items))()
+    for i, (x, w, ws, out) in enumerate(items):
+        arr[i] = W8A8Problem(_ptr(x), _ptr(w), _ptr(ws), _ptr(out), w.shape[0])
+    return arr
+
+
+def w8a8_fused_grouped(items=None, M: int = 1, K: int = None, problems=None, stream=None) -> None:
+    """Independent fused W8A8 GEMVs ([N,K] int8 weights) in one launch."""
+    arr = problems if problems is not None else w8a8_problems(items)
+    if K is None:
+        K = items[0][0].shape[1]
+        M = items[0][0].shape[0]
+    _check(lib().mcv_w8a8_fused_grouped(ctypes.cast(arr, _vp), len(arr), M, K, _stream(stream)), "w8a8_fused_grouped")
 
 
 def w8a8_fused(x, w_int8, w_scale, out, acc=None, x_int8=None, x_scale=None, w_layout: int = 0,

@@ -203,3 +203,23 @@ def test_prequant_gemv_equals_fused(cuda, M, N):
         assert np.array_equal(acc.cpu().numpy(), np.asarray(r_acc).reshape(M, N))
         assert np.array_equal(out.cpu().numpy().view(np.uint16), np.asarray(r_out).reshape(M, N))
     mcv.set_tuning(6, 0)
+
+
+@pytest.mark.parametrize("M", [1, 4])
+def test_grouped_fused_equals_single(cuda, M):
+    """Several fused W8A8 GEMVs in one launch (e.g. gate and up on one input):
+    each bit-exact against the oracle."""
+    import mcv_b200 as mcv
+    torch = cuda
+    items, refs = [], []
+    x, _, _ = synth.w8a8_inputs(M, 1024, 16, seed=90 + M)
+    xd = torch.from_numpy(x).cuda()
+    for i, N in enumerate((3584, 3584, 1024, 40)):
+        _, w, ws = synth.w8a8_inputs(M, 1024, N, seed=100 * M + i)
+        out = torch.zeros((M, N), dtype=torch.float16, device="cuda")
+        items.append((xd, torch.from_numpy(np.ascontiguousarray(w.T)).cuda(), torch.from_numpy(ws).cuda(), out))
+        refs.append(np.asarray(oracle.w8a8_fused(x, w, ws)[1]).reshape(M, N))
+    mcv.w8a8_fused_grouped(items)
+    torch.cuda.synchronize()
+    for (_, _, _, out), ref in zip(items, refs):
+        assert np.array_equal(out.cpu().numpy().view(np.uint16), ref)

@@ -102,6 +102,14 @@ def test_w8a8_arguments(L):
     assert L.mcv_w8a8_fused(F2, F, F, F, None, None, None, 1, 1024, 3584, 0, None) == ALIGN
     assert L.mcv_w8a8_fused(None, F, F, F, None, None, None, 1, 1024, 3584, 0, None) == NULL
     assert L.mcv_w8a8_quantize(F, F, F, 0, 1024, None) == SHAPE
+    P8 = mcv_b200.W8A8Problem
+    ok = P8(F, F, F, F, 3584)
+    arr = (P8 * 17)(*([ok] * 17))
+    assert L.mcv_w8a8_fused_grouped(arr, 0, 1, 1024, None) == NULL
+    assert L.mcv_w8a8_fused_grouped(arr, 17, 1, 1024, None) == SHAPE
+    assert L.mcv_w8a8_fused_grouped(arr, 2, 9, 1024, None) == SHAPE
+    arr[1] = P8(F2, F, F, F, 3584)
+    assert L.mcv_w8a8_fused_grouped(arr, 2, 1, 1024, None) == ALIGN
     assert L.mcv_w8a8_gemv_prequant(F, None, F, F, F, None, 1, 1024, 3584, None) == NULL
     assert L.mcv_w8a8_gemv_prequant(F, F, F, F, F, None, 9, 1024, 3584, None) == SHAPE
     assert L.mcv_w8a8_gemv_prequant(F2, F, F, F, F, None, 1, 1024, 3584, None) == ALIGN
