@@ -442,29 +442,19 @@ w4a16_tma_kernel(const __grid_constant__ GroupParams gp) {
         const uint32_t zlo = *reinterpret_cast<const uint32_t*>(st + kStageW + 128 + g * 4) >> sh;
         const uint32_t zhi = *reinterpret_cast<const uint32_t*>(st + kStageW + 128 + (g + 8) * 4) >> sh;
         const __half* xrow = P.x + static_cast<size_t>(g) * K + cur.c * kChunkK + 16 * t;
-        auto do_group = [&](int gi) {
+#pragma unroll
+        for (int gi = 0; gi < 4; ++gi) {
+            if (2 * gi >= nq) break;
             const uint4 v[2] = {*reinterpret_cast<const uint4*>(st + (2 * gi * 32 + lane) * 16),
                                 *reinterpret_cast<const uint4*>(st + ((2 * gi + 1) * 32 + lane) * 16)};
             float d[4];
             group_mma<M, MATH>(v, xrow + gi * kGroup, g, static_cast<int>((zlo >> (4 * gi)) & 0xfu) + P.zero_bias,
-                               static_cast<int>((zhi >> (4 * gi)) & 0xfu) + P.zero_bias, d);
+                         static_cast<int>((zhi >> (4 * gi)) & 0xfu) + P.zero_bias, d);
             const float s_lo = half_of(slo, gi), s_hi = half_of(shi, gi);
             acc[0] = fmaf(d[0], s_lo, acc[0]);
             acc[1] = fmaf(d[1], s_lo, acc[1]);
             acc[2] = fmaf(d[2], s_hi, acc[2]);
             acc[3] = fmaf(d[3], s_hi, acc[3]);
-        };
-        if (nq == 8) {
-            // a full 512-k chunk: no per-group exit test, so the four groups'
-            // loads and dequant can be scheduled across one another
-#pragma unroll
-            for (int gi = 0; gi < 4; ++gi) do_group(gi);
-        } else {
-#pragma unroll
-            for (int gi = 0; gi < 4; ++gi) {
-                if (2 * gi >= nq) break;
-                do_group(gi);
-            }
         }
         const int nchunks = (K + kChunkK - 1) / kChunkK;
         if (cur.c + 1 == nchunks) {
