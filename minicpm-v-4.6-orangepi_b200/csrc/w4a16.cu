@@ -223,10 +223,17 @@ struct GroupParams {
 };
 
 
+// The problem owning a global strip: a binary search over the problems'
+// first strips (at most 6 steps for 48 problems; a persistent warp's next
+// strip is ~W strips on, often many problems away).
 __device__ __forceinline__ int find_problem(const GroupParams& gp, int strip, int start) {
-    int pi = start;
-    while (pi + 1 < gp.count && strip >= gp.p[pi + 1].strip_begin) ++pi;
-    return pi;
+    int lo = start, hi = gp.count - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (gp.p[mid].strip_begin <= strip) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
 }
 
 // Register buffer of one (strip, 512-k chunk): eight lane vectors (32
