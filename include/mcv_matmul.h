@@ -81,7 +81,7 @@ void mcv_set_pdl(int enabled);
  *   there are fewer strips.
  *   MCV_TUNE_W4A16_MATH: the W4A16 GEMV's per-group arithmetic - 1 = exact
  *   (q - zero) per weight on four MMA chains, 2 = the same on two chains with
- *   integer-built zero constants, 3 = zero point folded out (raw
+ *   integer-built zero constants (default), 3 = zero point folded out (raw
  *   exponent-bias weights, sum(x) from an all-ones MMA). */
 enum mcv_tuning_key {
     MCV_TUNE_W4A16_MODE = 2,
