@@ -81,8 +81,9 @@ void mcv_set_pdl(int enabled);
  *   there are fewer strips.
  *   MCV_TUNE_W4A16_MATH: the W4A16 GEMV's per-group arithmetic - 1 = exact
  *   (q - zero) per weight on four MMA chains, 2 = the same on two chains with
- *   integer-built zero constants (default), 3 = zero point folded out (raw
- *   exponent-bias weights, sum(x) from an all-ones MMA). */
+ *   integer-built zero constants, 3 = zero point folded out (raw
+ *   exponent-bias weights, sum(x) from an all-ones MMA); default: 1 for the
+ *   K-split schedule, 2 for the bulk-copy ring. */
 enum mcv_tuning_key {
     MCV_TUNE_W4A16_MODE = 2,
     MCV_TUNE_ROWS_BLOCKS_PER_SM = 3,

@@ -85,12 +85,6 @@ __device__ __forceinline__ uint32_t h2_bits_neg_64_plus(int z) {
     return (0xD400u | (static_cast<uint32_t>(z) << 4)) * 0x10001u;
 }
 
-// The per-group arithmetic the GEMVs use by default (MCV_TUNE_W4A16_MATH 0):
-// integer-built zero constants and two MMA chains (variant 1 below), which
-// measured 3 % faster than four chains with converted constants in the
-// grouped launch (0.500 vs 0.516 us per config-0 GEMV).
-constexpr int kDefaultMath = 1;
-
 template <int M, int MATH>
 __device__ __forceinline__ void group_mma(const uint4 (&v)[2], const __half* xg, int g, int zl_q, int zh_q,
                                           float d[4]);
@@ -382,21 +376,23 @@ constexpr int kTmaSmem = kWarps * kRing * kStageBytes + kWarps * kRing * 8;
 
 static __device__ unsigned g_w4a16_dev_error;
 
-// A warp's walk over (strip, 512-k chunk) items: its own contiguous range of
-// strips [strip, end), each strip's chunks in order.  Consecutive strips
-// mostly belong to the same problem, so moving on is a comparison with the
-// next problem's first strip rather than a search, and the chunk count is
-// kept with the iterator.
+// A warp's walk over (strip, 512-k chunk) items: strips strided by the grid's
+// warp count (measured faster than one contiguous strip range per warp,
+// 0.50 vs 0.55 us per grouped GEMV), each strip's chunks in order; the chunk
+// count of the current problem rides along.
 struct ItemIter {
-    int strip, c, pi, nchunks, end;
+    int strip, c, pi, nchunks;
 };
 
-__device__ __forceinline__ void next_item(const GroupParams& gp, ItemIter& it, int /*W*/) {
+__device__ __forceinline__ int chunks_of(const GroupParams& gp, int pi) { return (gp.p[pi].K + kChunkK - 1) / kChunkK; }
+
+__device__ __forceinline__ void next_item(const GroupParams& gp, ItemIter& it, int W) {
     if (++it.c == it.nchunks) {
         it.c = 0;
-        if (++it.strip < it.end) {
-            while (it.pi + 1 < gp.count && it.strip >= gp.p[it.pi + 1].strip_begin) ++it.pi;
-            it.nchunks = (gp.p[it.pi].K + kChunkK - 1) / kChunkK;
+        it.strip += W;
+        if (it.strip < gp.total_strips) {
+            it.pi = find_problem(gp, it.strip, it.pi);
+            it.nchunks = chunks_of(gp, it.pi);
         }
     }
 }
@@ -429,15 +425,10 @@ w4a16_tma_kernel(const __grid_constant__ GroupParams gp) {
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * kRing * kStageBytes) + warp * kRing;
     const int W = static_cast<int>(gridDim.x) * kWarps;
     const int T = gp.total_strips;
-    // warp w of block b is global warp (w * gridDim.x + b), so neighbouring
-    // strip ranges start on different SMs
-    const int gw = warp * static_cast<int>(gridDim.x) + static_cast<int>(blockIdx.x);
-    const int begin = static_cast<int>(static_cast<int64_t>(gw) * T / W);
-    const int end = static_cast<int>(static_cast<int64_t>(gw + 1) * T / W);
-    ItemIter cur{begin, 0, 0, 1, end};
-    if (cur.strip < end) {
+    ItemIter cur{warp * static_cast<int>(gridDim.x) + static_cast<int>(blockIdx.x), 0, 0, 1};
+    if (cur.strip < T) {
         cur.pi = find_problem(gp, cur.strip, 0);
-        cur.nchunks = (gp.p[cur.pi].K + kChunkK - 1) / kChunkK;
+        cur.nchunks = chunks_of(gp, cur.pi);
     }
     if (lane == 0)
         for (int s = 0; s < kRing; ++s) mbar_init(&bars[s], 1 + 32);  // bulk arrival + 32 cp.async lanes
@@ -445,7 +436,7 @@ w4a16_tma_kernel(const __grid_constant__ GroupParams gp) {
     __syncwarp();
     ItemIter iss = cur;
     int issued = 0;
-    for (; issued < kRing && iss.strip < iss.end; ++issued) {
+    for (; issued < kRing && iss.strip < T; ++issued) {
         issue_item(gp, iss, ring + issued * kStageBytes, &bars[issued], lane);
         next_item(gp, iss, W);
     }
@@ -453,7 +444,7 @@ w4a16_tma_kernel(const __grid_constant__ GroupParams gp) {
     pdl_wait();  // x may be the previous kernel's output
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll 1
-    for (int k = 0; cur.strip < cur.end; ++k) {
+    for (int k = 0; cur.strip < T; ++k) {
         const int s = k % kRing;
         if (!mbar_wait(&bars[s], static_cast<uint32_t>(k / kRing) & 1u)) {
             if (lane == 0) atomicOr(&g_w4a16_dev_error, kDevErrTimeout);
@@ -490,7 +481,7 @@ w4a16_tma_kernel(const __grid_constant__ GroupParams gp) {
         // refill this stage with the item kRing ahead
         fence_proxy_async_smem();
         __syncwarp();
-        if (iss.strip < iss.end) {
+        if (iss.strip < T) {
             issue_item(gp, iss, ring + s * kStageBytes, &bars[s], lane);
             next_item(gp, iss, W);
         }
@@ -757,8 +748,8 @@ w4a16_gate_up_silu_kernel(const __grid_constant__ GroupParams gp) {
         const int gi = wq + j * kWarps;
         if (gi >= G) break;
         float d[4];
-        group_mma<M, kDefaultMath>(v[j], P.x + static_cast<size_t>(g) * K + gi * kGroup + 16 * t, g,
-                                   zlo[j] + P.zero_bias, zhi[j] + P.zero_bias, d);
+        group_mma<M>(v[j], P.x + static_cast<size_t>(g) * K + gi * kGroup + 16 * t, g, zlo[j] + P.zero_bias,
+                     zhi[j] + P.zero_bias, d);
         acc[0] = fmaf(d[0], slo[j], acc[0]);
         acc[1] = fmaf(d[1], slo[j], acc[1]);
         acc[2] = fmaf(d[2], shi[j], acc[2]);
@@ -809,8 +800,14 @@ int assign_strips(GroupParams& gp) {
     return t;
 }
 
-template <int M, int MATH>
+// MATH < 0: each schedule's measured default - the K-split kernel's
+// four-chain arithmetic (variant 0; 1.73 vs 1.76 us per dependent GEMV) and
+// the bulk-copy ring's two chains with integer-built zero constants (variant
+// 1; 0.500 vs 0.516 us per GEMV in a 48-GEMV launch).
+template <int M, int MATH_ARG>
 int launch_m(GroupParams& gp, cudaStream_t st) {
+    constexpr int MATH = MATH_ARG < 0 ? 0 : MATH_ARG;
+    constexpr int RING_MATH = MATH_ARG < 0 ? 1 : MATH_ARG;
     const int strips = assign_strips(gp);
     const int mode = tuning(MCV_TUNE_W4A16_MODE);
     // few strips: one block per strip with K split over its warps; many
@@ -833,7 +830,7 @@ int launch_m(GroupParams& gp, cudaStream_t st) {
         const int blocks = std::min(strips, sm_count() * kBlocksPerSm);
         return launch(w4a16_gemv_kernel<M>, dim3(blocks), dim3(kWarps * 32), 0, st, gp);
     }
-    auto kern = w4a16_tma_kernel<M, MATH>;
+    auto kern = w4a16_tma_kernel<M, RING_MATH>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTmaSmem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a16_tma)");
     // As many warps as fit (3 blocks of 8 per SM): the stream is bound by
@@ -867,7 +864,7 @@ int run_group(GroupParams& gp, int64_t M, cudaStream_t st) {
         case 1: return run_group_math<0>(gp, M, st);
         case 2: return run_group_math<1>(gp, M, st);
         case 3: return run_group_math<2>(gp, M, st);
-        default: return run_group_math<kDefaultMath>(gp, M, st);
+        default: return run_group_math<-1>(gp, M, st);
     }
 }
 
