@@ -83,7 +83,9 @@ void mcv_set_pdl(int enabled);
  *   (q - zero) per weight on four MMA chains, 2 = the same on two chains with
  *   integer-built zero constants, 3 = zero point folded out (raw
  *   exponent-bias weights, sum(x) from an all-ones MMA); default: 1 for the
- *   K-split schedule, 2 for the bulk-copy ring. */
+ *   K-split schedule, 2 for the bulk-copy ring.
+ *   MCV_TUNE_W4A16_KSPLIT_WARPS: warps per strip of the K-split W4A16 kernel
+ *   (8, 16 or 32; arithmetic 1 only); default 8 up to K = 1024, else 16. */
 enum mcv_tuning_key {
     MCV_TUNE_W4A16_MODE = 2,
     MCV_TUNE_ROWS_BLOCKS_PER_SM = 3,
@@ -93,7 +95,8 @@ enum mcv_tuning_key {
     MCV_TUNE_W4A16_GRID = 7,
     MCV_TUNE_W4A16_MATH = 8,
     MCV_TUNE_ROWS_WALK = 9,
-    MCV_TUNE_COUNT = 10
+    MCV_TUNE_W4A16_KSPLIT_WARPS = 10,
+    MCV_TUNE_COUNT = 11
 };
 int mcv_set_tuning(int key, int value);
 /* Device-side error bits recorded since the last call (and cleared by it):

@@ -16,8 +16,8 @@
 //    fragments of four MMAs, and a warp-wide load reads 512 contiguous bytes.
 //  * Work.  Three schedules (MCV_TUNE_W4A16_MODE picks one explicitly):
 //    - K-split (default for a launch with few strips, i.e. one decode GEMV):
-//      one block per strip, its 8 warps take the strip's 128-k groups and
-//      meet in shared memory - one load latency on the critical path;
+//      one block per strip, its 8 or 16 warps take the strip's 128-k groups
+//      and meet in shared memory - one load latency on the critical path;
 //    - bulk-copy streaming (default for large launches): a persistent grid,
 //      each warp owns whole strips and walks them in 512-k chunks that land
 //      in a warp-private 2-deep cp.async.bulk ring while the previous chunk
@@ -491,15 +491,16 @@ w4a16_tma_kernel(const __grid_constant__ GroupParams gp) {
 
 // ---------------------------------------------------------------------------
 // K-split variant for launches with few strips (a single decode GEMV): one
-// block per strip, its 8 warps take the strip's 128-k groups round-robin (at
-// most KG each), load all their weight vectors, scales and zeros before
-// griddepcontrol.wait, and meet in shared memory for the final sum.  This
-// keeps a lone GEMV's critical path to one load latency plus 1/8 of its math.
+// block per strip, its W warps (8, or 16 above 1024 k) take the strip's 128-k
+// groups round-robin (at most KG each), load all their weight vectors, scales
+// and zeros before griddepcontrol.wait, and meet in shared memory for the
+// final sum.  This keeps a lone GEMV's critical path to one load latency plus
+// 1/W of its math.
 // ---------------------------------------------------------------------------
-template <int M, int KG, int MATH>
-__global__ void __launch_bounds__(kWarps * 32)
+template <int M, int KG, int MATH, int W>
+__global__ void __launch_bounds__(W * 32)
 w4a16_ksplit_kernel(const __grid_constant__ GroupParams gp) {
-    __shared__ float4 red[kWarps][32];
+    __shared__ float4 red[W][32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int strip = static_cast<int>(blockIdx.x);
@@ -513,7 +514,7 @@ w4a16_ksplit_kernel(const __grid_constant__ GroupParams gp) {
     int zlo[KG], zhi[KG];
 #pragma unroll
     for (int j = 0; j < KG; ++j) {
-        const int gi = warp + j * kWarps;
+        const int gi = warp + j * W;
         v[j][0] = v[j][1] = make_uint4(0, 0, 0, 0);
         slo[j] = shi[j] = 0.0f;
         zlo[j] = zhi[j] = 0;
@@ -532,7 +533,7 @@ w4a16_ksplit_kernel(const __grid_constant__ GroupParams gp) {
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int j = 0; j < KG; ++j) {
-        const int gi = warp + j * kWarps;
+        const int gi = warp + j * W;
         if (gi >= G) break;
         float d[4];
         group_mma<M, MATH>(v[j], P.x + static_cast<size_t>(g) * K + gi * kGroup + 16 * t, g, zlo[j] + P.zero_bias,
@@ -547,7 +548,7 @@ w4a16_ksplit_kernel(const __grid_constant__ GroupParams gp) {
     if (warp == 0) {
         float4 sum = red[0][lane];
 #pragma unroll
-        for (int w = 1; w < kWarps; ++w) {
+        for (int w = 1; w < W; ++w) {
             const float4 r = red[w][lane];
             sum.x += r.x;
             sum.y += r.y;
@@ -702,23 +703,22 @@ int run_group_wide(GroupParams& gp, int M, cudaStream_t st) {
 
 // The MLP's gate and up projections with SwiGLU in the epilogue
 // (decoder_layer.cpp:1186-1203): act = silu_mul(x . Wg, x . Wu).  Block b
-// computes strip b of both weights with 16 warps - warps 0-7 the gate, 8-15
-// the up projection, each half splitting K exactly as the K-split kernel does,
+// computes strip b of both weights with 2W warps - warps 0..W-1 the gate,
+// W..2W-1 the up projection (W = 8, or 16 above 1024 k), each half splitting
+// K exactly as the K-split kernel does,
 // so the sums (and, after rounding to fp16, the projections' outputs) are the
 // separate GEMVs' bit for bit.  silu_mul's arithmetic then runs on the two
 // fp16 values, so one launch replaces the gate/up launch plus the silu_mul
 // launch, and the fp16 gate and up never travel through memory.
-constexpr int kGUWarps = 2 * kWarps;
-
-template <int M, int KG>
-__global__ void __launch_bounds__(kGUWarps * 32)
+template <int M, int KG, int W>
+__global__ void __launch_bounds__(2 * W * 32)
 w4a16_gate_up_silu_kernel(const __grid_constant__ GroupParams gp) {
-    __shared__ float4 red[kGUWarps][32];
+    __shared__ float4 red[2 * W][32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int strip = static_cast<int>(blockIdx.x);
-    const int wq = warp & (kWarps - 1);
-    const Problem& P = gp.p[warp / kWarps];  // 0: gate, 1: up
+    const int wq = warp & (W - 1);
+    const Problem& P = gp.p[warp / W];  // 0: gate, 1: up
     const int K = P.K, G = K / kGroup, Gp = (G + 7) & ~7, zw = (G + 7) >> 3;
     const int col = strip * 16 + g;
     uint4 v[KG][2];
@@ -726,7 +726,7 @@ w4a16_gate_up_silu_kernel(const __grid_constant__ GroupParams gp) {
     int zlo[KG], zhi[KG];
 #pragma unroll
     for (int j = 0; j < KG; ++j) {
-        const int gi = wq + j * kWarps;
+        const int gi = wq + j * W;
         v[j][0] = v[j][1] = make_uint4(0, 0, 0, 0);
         slo[j] = shi[j] = 0.0f;
         zlo[j] = zhi[j] = 0;
@@ -745,7 +745,7 @@ w4a16_gate_up_silu_kernel(const __grid_constant__ GroupParams gp) {
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int j = 0; j < KG; ++j) {
-        const int gi = wq + j * kWarps;
+        const int gi = wq + j * W;
         if (gi >= G) break;
         float d[4];
         group_mma<M>(v[j], P.x + static_cast<size_t>(g) * K + gi * kGroup + 16 * t, g, zlo[j] + P.zero_bias,
@@ -758,10 +758,10 @@ w4a16_gate_up_silu_kernel(const __grid_constant__ GroupParams gp) {
     red[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
     __syncthreads();
     if (warp == 0) {
-        float4 gs = red[0][lane], us = red[kWarps][lane];
+        float4 gs = red[0][lane], us = red[W][lane];
 #pragma unroll
-        for (int w = 1; w < kWarps; ++w) {
-            const float4 a = red[w][lane], b = red[kWarps + w][lane];
+        for (int w = 1; w < W; ++w) {
+            const float4 a = red[w][lane], b = red[W + w][lane];
             gs.x += a.x, gs.y += a.y, gs.z += a.z, gs.w += a.w;
             us.x += b.x, us.y += b.y, us.z += b.z, us.w += b.w;
         }
@@ -783,11 +783,18 @@ template <int M>
 int launch_gate_up_m(GroupParams& gp, cudaStream_t st) {
     const int strips = static_cast<int>(padded_n(gp.p[0].N) / 16);
     const int G = gp.p[0].K / kGroup;
-    const int per_warp = (G + kWarps - 1) / kWarps;
-    auto go = [&](auto kern) { return launch(kern, dim3(strips), dim3(kGUWarps * 32), 0, st, gp); };
-    if (per_warp <= 1) return go(w4a16_gate_up_silu_kernel<M, 1>);
-    if (per_warp <= 2) return go(w4a16_gate_up_silu_kernel<M, 2>);
-    return go(w4a16_gate_up_silu_kernel<M, 4>);
+    // warps per half as the single-GEMV kernel picks them (8, or 16 above
+    // 1024 k), so the two give the same sums
+    const int W = G > kWarps ? 2 * kWarps : kWarps;
+    const int per_warp = (G + W - 1) / W;
+    auto go = [&](auto kern) { return launch(kern, dim3(strips), dim3(2 * W * 32), 0, st, gp); };
+    if (W == kWarps) {
+        if (per_warp <= 1) return go(w4a16_gate_up_silu_kernel<M, 1, kWarps>);
+        if (per_warp <= 2) return go(w4a16_gate_up_silu_kernel<M, 2, kWarps>);
+        return go(w4a16_gate_up_silu_kernel<M, 4, kWarps>);
+    }
+    if (per_warp <= 1) return go(w4a16_gate_up_silu_kernel<M, 1, 2 * kWarps>);
+    return go(w4a16_gate_up_silu_kernel<M, 2, 2 * kWarps>);
 }
 
 int assign_strips(GroupParams& gp) {
@@ -817,12 +824,31 @@ int launch_m(GroupParams& gp, cudaStream_t st) {
     if (mode == 2 || (mode == 0 && strips < sm_count() * 4)) {
         int maxG = 0;
         for (int i = 0; i < gp.count; ++i) maxG = std::max(maxG, gp.p[i].K / kGroup);
-        const int per_warp = (maxG + kWarps - 1) / kWarps;
-        auto go = [&](auto kern) { return launch(kern, dim3(strips), dim3(kWarps * 32), 0, st, gp); };
-        if (per_warp <= 1) return go(w4a16_ksplit_kernel<M, 1, MATH>);
-        if (per_warp <= 2) return go(w4a16_ksplit_kernel<M, 2, MATH>);
-        if (per_warp <= 4) return go(w4a16_ksplit_kernel<M, 4, MATH>);
-        if (per_warp <= 8) return go(w4a16_ksplit_kernel<M, 8, MATH>);
+        const int tw = tuning(MCV_TUNE_W4A16_KSPLIT_WARPS);
+        // warps per strip: one per 128-k group up to 16 (K = 2048 / 3584 on 16
+        // warps: more loads in flight per strip before the wait; measured on
+        // the decode step's launch sequence); MCV_TUNE_W4A16_KSPLIT_WARPS
+        // = 8 / 16 / 32 forces one
+        int W = maxG > kWarps ? 2 * kWarps : kWarps;
+        if (tw == 8 || tw == 16 || tw == 32) W = tw;
+        if (MATH != 0) W = kWarps;
+        const int per_warp = (maxG + W - 1) / W;
+        auto go = [&](auto kern, int w) { return launch(kern, dim3(strips), dim3(w * 32), 0, st, gp); };
+        if (W == 8) {
+            if (per_warp <= 1) return go(w4a16_ksplit_kernel<M, 1, MATH, 8>, 8);
+            if (per_warp <= 2) return go(w4a16_ksplit_kernel<M, 2, MATH, 8>, 8);
+            if (per_warp <= 4) return go(w4a16_ksplit_kernel<M, 4, MATH, 8>, 8);
+            if (per_warp <= 8) return go(w4a16_ksplit_kernel<M, 8, MATH, 8>, 8);
+        } else if constexpr (MATH == 0) {
+            if (W == 16) {
+                if (per_warp <= 1) return go(w4a16_ksplit_kernel<M, 1, 0, 16>, 16);
+                if (per_warp <= 2) return go(w4a16_ksplit_kernel<M, 2, 0, 16>, 16);
+                if (per_warp <= 4) return go(w4a16_ksplit_kernel<M, 4, 0, 16>, 16);
+            } else {
+                if (per_warp <= 1) return go(w4a16_ksplit_kernel<M, 1, 0, 32>, 32);
+                if (per_warp <= 2) return go(w4a16_ksplit_kernel<M, 2, 0, 32>, 32);
+            }
+        }
         // larger K: the streaming kernel has no K limit
     }
     if (mode == 1) {

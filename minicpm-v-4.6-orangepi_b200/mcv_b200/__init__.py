@@ -174,6 +174,7 @@ TUNE_W8A8_KERNEL = 6
 TUNE_W4A16_GRID = 7
 TUNE_W4A16_MATH = 8
 TUNE_ROWS_WALK = 9
+TUNE_W4A16_KSPLIT_WARPS = 10
 
 
 def device_errors() -> int:
