@@ -176,10 +176,10 @@ int mcv_w4a16_pack_from_tiles_host(const int8_t* packed, int64_t tile_len,
                                    uint32_t* qweight_out, uint16_t* scales_out,
                                    uint32_t* zeros_out, int* zero_bias_out);
 
-/* out[m][n] = sum_k x[m][k] * w[k][n], M = 1..32, fp32 accumulation, fp16 out.
+/* out[m][n] = sum_k x[m][k] * w[k][n], M = 1..64, fp32 accumulation, fp16 out.
  * x fp16 [M][K], out fp16 [M][N]; group must be 128; x, qweight and scales
- * 16-byte aligned.  M = 9..32 (batched decode) shares each dequantised weight
- * fragment across up to four MMAs and needs K <= 8192.
+ * 16-byte aligned.  M = 9..64 (batched decode) shares each dequantised weight
+ * fragment across up to eight MMAs and needs K <= 8192.
  * Replaces matmul_w4a16 (src/csrc/lib/ops.cpp:1030-1095, ops.h:95-108; M=1
  * there) and its kernel op_kernel/matmul_w4a16_custom.cpp. */
 int mcv_w4a16_gemv(const void* x, const void* qweight, const void* scales, const void* zeros,

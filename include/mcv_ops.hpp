@@ -69,14 +69,14 @@ void need_rank2(const T& t, const char* what) {
 }
 }  // namespace detail
 
-/* out [M,N] = x [M,K] . W for the packed int4 weight (M = 1..32 on the GEMV,
- * larger M on the tensor-core GEMM).  ops.h:104-108. */
+/* out [M,N] = x [M,K] . W for the packed int4 weight (the GEMV up to 32 rows,
+ * or 64 rows with K <= 4096; the tensor-core GEMM beyond).  ops.h:104-108. */
 template <class T>
 void matmul_w4a16(const T& x, const W4A16Weight& w, T& out, cudaStream_t stream, bool sync = false) {
     detail::need_rank2(x, "matmul_w4a16");
     const int64_t M = x.shape()[0], K = x.shape()[1];
     if (K != w.K) throw Error(MCV_ERR_SHAPE, "matmul_w4a16: x and weight K differ");
-    const int st = M <= 32 ? mcv_w4a16_gemv(x.data(), w.qweight, w.scales, w.zeros, w.zero_bias, out.data(), M, K,
+    const int st = (M <= 32 || (M <= 64 && K <= 4096)) ? mcv_w4a16_gemv(x.data(), w.qweight, w.scales, w.zeros, w.zero_bias, out.data(), M, K,
                                            w.N, 128, stream)
                           : mcv_w4a16_gemm(x.data(), w.qweight, w.scales, w.zeros, w.zero_bias, out.data(), M, K,
                                            w.N, 128, stream);

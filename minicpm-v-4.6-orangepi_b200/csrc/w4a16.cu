@@ -1,4 +1,4 @@
-// W4A16 GEMV for decode (M = 1..8) over the mcv-int4 weight layout, plus the
+// W4A16 GEMV for decode (M = 1..8, batched up to 64) over the mcv-int4 weight layout, plus the
 // load-time host repackers from GPTQ / AWQ / the reference's tile layout.
 //
 // Reference behaviour replaced: matmul_w4a16 (src/csrc/lib/ops.cpp:1030-1095)
@@ -51,6 +51,7 @@ constexpr int kChunkK = 512;       // k per register buffer (8 lane vectors, 4 g
 constexpr int kWarps = 8;
 constexpr int kBlocksPerSm = 2;
 constexpr int kMaxGroupProblems = 48;
+constexpr int kMaxGemvRows = 64;  // rows of x on the GEMV schedules (M > 8: up to 8 MMAs per fragment)
 
 __host__ __device__ inline int64_t padded_n(int64_t N) { return (N + 15) / 16 * 16; }
 __host__ __device__ inline int64_t padded_g(int64_t G) { return (G + 7) / 8 * 8; }
@@ -560,9 +561,9 @@ w4a16_ksplit_kernel(const __grid_constant__ GroupParams gp) {
     }
 }
 
-// Batched decode, M = 9..32 rows of x: the K-split schedule with each
+// Batched decode, M = 9..64 rows of x: the K-split schedule with each
 // dequantised A fragment feeding MT = ceil(M / 8) MMAs, one per 8 rows of x
-// (the MMA's N), so the dequant work per weight is paid once for up to 32
+// (the MMA's N), so the dequant work per weight is paid once for up to 64
 // rows.  Lane (g, t) supplies x row 8T + g of tile T and ends with the
 // outputs of rows 8T + 2t, 8T + 2t + 1 for columns g, g + 8 of the strip.
 template <int MT, int KG>
@@ -698,7 +699,9 @@ int launch_wide_mt(GroupParams& gp, int M, cudaStream_t st) {
 int run_group_wide(GroupParams& gp, int M, cudaStream_t st) {
     if (M <= 16) return launch_wide_mt<2>(gp, M, st);
     if (M <= 24) return launch_wide_mt<3>(gp, M, st);
-    return launch_wide_mt<4>(gp, M, st);
+    if (M <= 32) return launch_wide_mt<4>(gp, M, st);
+    if (M <= 48) return launch_wide_mt<6>(gp, M, st);
+    return launch_wide_mt<8>(gp, M, st);
 }
 
 // The MLP's gate and up projections with SwiGLU in the epilogue
@@ -1144,7 +1147,7 @@ int mcv_w4a16_gemv_gate_up_silu(const void* x, const mcv_w4a16_problem* gate, co
 
 int mcv_w4a16_gemv_grouped(const mcv_w4a16_problem* problems, int count, int64_t M, mcv_stream_t stream) {
     if (!problems || count < 1) return fail(MCV_ERR_NULL, "w4a16_gemv: no problems");
-    if (M < 1 || M > 32) return fail(MCV_ERR_SHAPE, "w4a16_gemv: M must be 1..32");
+    if (M < 1 || M > kMaxGemvRows) return fail(MCV_ERR_SHAPE, "w4a16_gemv: M must be 1..64");
     for (int i = 0; i < count; ++i) {
         const mcv_w4a16_problem& p = problems[i];
         if (!p.x || !p.qweight || !p.scales || !p.zeros || !p.out) return fail(MCV_ERR_NULL, "w4a16_gemv: null pointer");

@@ -397,7 +397,7 @@ def load_w4a16_quantized_weight(st: SafeTensors, base: str, device="cuda") -> W4
 
 
 def matmul_w4a16(x, w: W4A16QuantizedWeight, out, stream=None) -> None:
-    """out fp16 [M,N] = x fp16 [M,K] @ dequant(w); M = 1..32 (ops.h:95-108)."""
+    """out fp16 [M,N] = x fp16 [M,K] @ dequant(w); M = 1..64 (ops.h:95-108)."""
     M = x.shape[0] if x.dim() == 2 else 1
     _check(lib().mcv_w4a16_gemv(_ptr(x), _ptr(w.qweight), _ptr(w.scales), _ptr(w.zeros), w.zero_bias, _ptr(out),
                                 M, w.K, w.N, w.group_size, _stream(stream)), "matmul_w4a16")

@@ -75,13 +75,15 @@ def test_dense_for_several_rows(formats):
     assert torch.equal(got, want)
 
 
-@pytest.mark.parametrize("M", [2, 8, 40])
+@pytest.mark.parametrize("M", [2, 8, 40, 80])
 def test_int4_without_dense_weight(formats, M):
+    """The int4 GEMV up to 32 rows (64 with K <= 4096), the tensor-core GEMM
+    beyond."""
     _, w4, _, _ = formats
     mcv.set_w8a8_decode_mode("0")
     x = xs(M, 4 + M)
     got = run(x, mcv.DecodeWeights.of(w4=w4))
-    if M <= 8:
+    if M <= 32 or (M <= 64 and w4.K <= 4096):
         want = direct(lambda o: mcv.matmul_w4a16(x, w4, o), M)
     else:
         want = direct(lambda o: mcv.matmul_w4a16_gemm(x, w4, o), M)

@@ -207,9 +207,10 @@ def test_no_device_errors_recorded(cuda):
 
 
 @pytest.mark.parametrize("M,K,N", [(9, 1024, 3584), (16, 1024, 4096), (24, 3584, 1024), (32, 1024, 3584),
-                                   (13, 8192, 64), (32, 128, 40)])
+                                   (13, 8192, 64), (32, 128, 40), (33, 1024, 520), (48, 2048, 1024),
+                                   (64, 1024, 3584), (57, 8192, 40)])
 def test_batched_decode_gemv(cuda, M, K, N):
-    """M = 9..32 on the widened GEMV (one dequantised fragment, up to four MMAs)."""
+    """M = 9..64 on the widened GEMV (one dequantised fragment, up to eight MMAs)."""
     import mcv_b200
     x, q, z, s = synth.w4a16_inputs(M, K, N, seed=M * 100 + K)
     ref = oracle.w4a16_gemv(x, oracle.w4a16_fold_zeros(q, z), s, nthreads=8)

@@ -70,7 +70,7 @@ def test_status_strings_and_errors_without_device():
     st = L.mcv_w4a16_gemv(None, None, None, None, 0, None, 1, 1024, 3584, 128, None)
     assert st == 1 and b"null" in L.mcv_last_error()
     fake = ctypes.c_void_p(16)
-    st = L.mcv_w4a16_gemv(fake, fake, fake, fake, 0, fake, 33, 1024, 3584, 128, None)
+    st = L.mcv_w4a16_gemv(fake, fake, fake, fake, 0, fake, 65, 1024, 3584, 128, None)
     assert st == 2
     st = L.mcv_w4a16_gemv(fake, fake, fake, fake, 0, fake, 1, 1000, 3584, 128, None)
     assert st == 2

@@ -34,7 +34,7 @@ def test_w4a16_grouped_arguments(L):
     good = P(F, F, F, F, F, 1024, 3584, 128, 0)
     arr = (P * 2)(good, good)
     assert L.mcv_w4a16_gemv_grouped(arr, 0, 1, None) == NULL
-    assert L.mcv_w4a16_gemv_grouped(arr, 2, 33, None) == SHAPE
+    assert L.mcv_w4a16_gemv_grouped(arr, 2, 65, None) == SHAPE
     arr[1] = P(F, F, F, None, F, 1024, 3584, 128, 0)
     assert L.mcv_w4a16_gemv_grouped(arr, 2, 1, None) == NULL
     arr[1] = P(F, F, F, F, F, 1000, 3584, 128, 0)
