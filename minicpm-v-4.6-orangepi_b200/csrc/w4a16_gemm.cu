@@ -66,6 +66,7 @@ constexpr int kTmemCols = 512;              // accumulator + A ring, rounded to 
 static_assert(kAccCols + kStages * kACols <= kTmemCols, "tensor memory budget");
 constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+static_assert(kXRows * kWCols * 4 + 16 <= kStages * kStageBytes, "split-k partials (and the failure word) must fit the ring");
 
 static __device__ unsigned g_gemm_dev_error;
 
