@@ -162,17 +162,32 @@ dense_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
     if (!acc_ready && tid == 0) atomicOr(&g_dense_gemm_dev_error, kDevErrTimeout);
     const uint32_t acc_lanes = tmem_acc + (static_cast<uint32_t>(warp * 32) << 16);
     if (a.splits == 1) {
-        if (acc_ready && warp < kDEpiWarps) {
-            const int col = n0 + warp * 32 + lane;
+        // fp16 outputs through a shared-memory tile (the ring is idle: every
+        // copy landed, every MMA completed), then 16-byte stores of 8
+        // columns instead of one 2-byte store per column and row
+        __half* tile = reinterpret_cast<__half*>(smem);  // [rows][kDW]
+        if (warp < kDEpiWarps) {
+            if (acc_ready) {
 #pragma unroll 1
-            for (int j = 0; j * 16 < mma_n; ++j) {
-                float v[16];
-                tmem_ld16(acc_lanes + j * 16, v);
-                if (col < a.N) {
+                for (int j = 0; j * 16 < mma_n; ++j) {
+                    float v[16];
+                    tmem_ld16(acc_lanes + j * 16, v);
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const int m = m0 + j * 16 + e;
-                        if (m < a.M) a.out[static_cast<size_t>(m) * a.N + col] = __float2half_rn(v[e]);
+                    for (int e = 0; e < 16; ++e) tile[(j * 16 + e) * kDW + warp * 32 + lane] = __float2half_rn(v[e]);
+                }
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(kDEpiWarps * 32) : "memory");  // the epilogue warps only
+            if (acc_ready) {
+                const bool vec_ok = (a.N & 7) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15u) == 0;
+                for (int idx = tid; idx < rows * (kDW / 8); idx += kDEpiWarps * 32) {
+                    const int r = idx / (kDW / 8), c8 = (idx % (kDW / 8)) * 8, col = n0 + c8;
+                    const __half* src = tile + r * kDW + c8;
+                    __half* o = a.out + static_cast<size_t>(m0 + r) * a.N + col;
+                    if (vec_ok && col + 8 <= a.N) {
+                        *reinterpret_cast<uint4*>(o) = *reinterpret_cast<const uint4*>(src);
+                    } else {
+                        for (int e = 0; e < 8; ++e)
+                            if (col + e < a.N) o[e] = src[e];
                     }
                 }
             }

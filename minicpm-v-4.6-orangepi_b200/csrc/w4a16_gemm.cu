@@ -299,17 +299,33 @@ w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
         // warp w reads TMEM lanes 32(w%4).. (weight columns) over columns
         // 16 j.. (rows of x) for j = w/4, w/4 + 4, ...; the issuer waited
         // for the last commit
-        const int col = n0 + quarter * 32 + lane;
-        if (acc_ready && warp < kDqWarps) {
+        // fp16 outputs through a shared-memory tile (the ring is idle now:
+        // every copy landed and every MMA completed), then 16-byte stores
+        // of 8 columns: an eighth of the store instructions of writing each
+        // thread's column directly (M = 1024, N = 4096: 12.1 vs 12.7 us)
+        __half* tile = reinterpret_cast<__half*>(smem);  // [rows][kWCols]
+        if (warp < kDqWarps) {
+            if (acc_ready) {
 #pragma unroll 1
-            for (int j = warp >> 2; j * 16 < mma_n; j += kDqWarps / 4) {
-                float v[16];
-                tmem_ld16(acc_lanes + j * 16, v);
-                if (col < a.N) {
+                for (int j = warp >> 2; j * 16 < mma_n; j += kDqWarps / 4) {
+                    float v[16];
+                    tmem_ld16(acc_lanes + j * 16, v);
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const int m = m0 + j * 16 + e;
-                        if (m < a.M) a.out[static_cast<size_t>(m) * a.N + col] = __float2half_rn(v[e]);
+                    for (int e = 0; e < 16; ++e) tile[(j * 16 + e) * kWCols + quarter * 32 + lane] = __float2half_rn(v[e]);
+                }
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(kDqThreads) : "memory");  // the dequantising warps only
+            if (acc_ready) {
+                const bool vec_ok = (a.N & 7) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15u) == 0;
+                for (int idx = tid; idx < rows * (kWCols / 8); idx += kDqThreads) {
+                    const int r = idx / (kWCols / 8), c8 = (idx % (kWCols / 8)) * 8, col = n0 + c8;
+                    const __half* src = tile + r * kWCols + c8;
+                    __half* o = a.out + static_cast<size_t>(m0 + r) * a.N + col;
+                    if (vec_ok && col + 8 <= a.N) {
+                        *reinterpret_cast<uint4*>(o) = *reinterpret_cast<const uint4*>(src);
+                    } else {
+                        for (int e = 0; e < 8; ++e)
+                            if (col + e < a.N) o[e] = src[e];
                     }
                 }
             }
