@@ -38,7 +38,7 @@ def test_gemm_vs_oracle(cuda, M, K):
     assert_f16_close(got, ref, what=f"gemm M={M} K={K}")
 
 
-@pytest.mark.parametrize("M,K,N", [(9, 128, 40), (100, 192, 136), (300, 512, 520), (17, 64, 8)])
+@pytest.mark.parametrize("M,K,N", [(9, 128, 40), (100, 192, 136), (300, 512, 520), (17, 64, 8), (33, 256, 1000)])
 def test_ragged_shapes(cuda, M, K, N):
     r = synth.rng(M * 3 + N)
     x = r.standard_normal((M, K), dtype=np.float32).astype(np.float16)

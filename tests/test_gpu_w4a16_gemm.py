@@ -22,7 +22,7 @@ def run(torch, x, w):
 
 @pytest.mark.parametrize("M,K,N", [(16, 1024, 3584), (64, 1024, 4096), (256, 1024, 3584), (1024, 1024, 4096),
                                    (100, 2048, 1000), (1, 128, 16), (130, 3584, 1024),
-                                   (300, 4096, 520)])
+                                   (300, 4096, 520), (70, 1024, 1001)])
 def test_gemm_vs_oracle(cuda, M, K, N):
     import mcv_b200
     x, q, z, s = synth.w4a16_inputs(M, K, N, seed=M + K + N)
