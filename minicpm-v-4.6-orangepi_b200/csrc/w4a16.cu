@@ -449,6 +449,10 @@ w4a16_tma_kernel(const __grid_constant__ GroupParams gp) {
         const int s = k % kRing;
         if (!mbar_wait(&bars[s], static_cast<uint32_t>(k / kRing) & 1u)) {
             if (lane == 0) atomicOr(&g_w4a16_dev_error, kDevErrTimeout);
+            // let this warp's other copies in flight land (each wait bounded)
+            // before the block can leave and its shared memory be reused
+            for (int it = k + 1; it < issued; ++it)
+                (void)mbar_wait(&bars[it % kRing], static_cast<uint32_t>(it / kRing) & 1u);
             return;
         }
         const Problem& P = gp.p[cur.pi];
@@ -485,6 +489,7 @@ w4a16_tma_kernel(const __grid_constant__ GroupParams gp) {
         if (iss.strip < T) {
             issue_item(gp, iss, ring + s * kStageBytes, &bars[s], lane);
             next_item(gp, iss, W);
+            ++issued;
         }
         next_item(gp, cur, W);
     }
